@@ -1,0 +1,400 @@
+"""Benchmark of the fused diagonal-covariance EM iteration on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl flashgmm|reference]
+                    [--workload c2]
+
+One *step* is one EM iteration (Pass 1 + Pass 2 statistics, stats allreduce when
+N > 1, M-step update) over the workload's points, inputs resident in HBM.  The
+metric is EM iterations/s of the named workload (default ``c2``: N=65,536,
+K=256, d=128).  With --gpus N > 1 (launched under torch.distributed.run, one
+rank per GPU, NCCL) every rank owns a full c2-sized shard of one larger data
+set (weak scaling) and ``value`` counts c2-sized iterations completed by all
+ranks per second.
+
+Rank 0 prints ONE JSON line.  Besides the contract keys it carries ``roofline``
+(dominant kernel, CUDA-event timed inside this run), ``cpu_baseline`` (the
+reference's own C++/OpenMP op on this host's cores, N=1 only), ``e2e`` (whole
+``NativeFlashGMM.fit`` calls from pinned host memory), ``clocks`` (nvidia-smi
+sampled during the timed region) and ``gpu_launches``.
+
+``--impl reference`` times the reference's CPU implementation of the same step
+(``oracle/_ref``, built from the reference sources; else the C restatement) on
+the host cores, rank 0 only.
+"""
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+from flashgmm_b200.data import WORKLOADS, make_workload  # noqa: E402
+
+FIT_ITERS = 20
+L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+
+
+# --------------------------------------------------------------------------- utils
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])),
+                "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+                "source": "fallback"}
+
+
+def algorithmic(wl, n_points):
+    """Per-iteration contraction FLOPs (12 N K d) and minimum HBM bytes
+    4 (N d + N + 4 K d + 2 K)."""
+    flops = 12.0 * n_points * wl.K * wl.d
+    nbytes = 4.0 * (n_points * wl.d + n_points + 4 * wl.K * wl.d + 2 * wl.K)
+    return flops, nbytes
+
+
+class ClockSampler:
+    """nvidia-smi samples (200 ms) of SM clock and throttle reasons during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.idx)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thr = threading.Thread(target=self._read, daemon=True)
+            self.thr.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.thr.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def gpu_id(dev):
+    """nvidia-smi -i selector for a torch device (UUID: immune to CUDA_VISIBLE_DEVICES)."""
+    try:
+        u = str(torch.cuda.get_device_properties(dev).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        return str(dev.index or 0)
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# ------------------------------------------------------------------ reference arm
+def load_reference_op():
+    """The reference's own CPU op (oracle/_ref) or, if it is not built, the C restatement."""
+    try:
+        from oracle.build_ref import load_ref
+        R = load_ref()
+        return (lambda X, mu, var, lp: R.flash_em_fused(X, mu, var, lp, 64, 8)), "reference"
+    except Exception:
+        from oracle import oracle
+        return (lambda X, mu, var, lp: [torch.from_numpy(a) for a in
+                                        oracle.flash_em_fused(X, mu, var, lp, BK=8)]), "port"
+
+
+def cpu_time_per_iter(wl, budget_s=12.0, min_iters=2):
+    """Time the reference CPU op on a bounded sample of the workload.  Returns
+    (seconds per full-size iteration, sample description, kind, threads)."""
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    op, kind = load_reference_op()
+    # size the sample so one iteration takes ~budget/4
+    n = min(wl.N, 4096)
+    X, mu, var, lp = make_workload(wl, N=n)
+    t0 = time.perf_counter()
+    op(X, mu, var, lp)
+    t1 = time.perf_counter() - t0
+    per_point = t1 / n
+    n = int(min(wl.N, max(1024, (budget_s / 4) / max(per_point, 1e-12))))
+    X, mu, var, lp = make_workload(wl, N=n)
+    its, t_tot = 0, 0.0
+    while its < min_iters or t_tot < budget_s * 0.5:
+        t0 = time.perf_counter()
+        mu, var, lp, ln = op(X, mu, var, lp)
+        t_tot += time.perf_counter() - t0
+        its += 1
+        if t_tot > budget_s:
+            break
+    s_iter_sample = t_tot / its
+    s_iter_full = s_iter_sample * wl.N / n  # cost is exactly linear in N
+    sample = (f"{its} iterations at N={n} of workload {wl.name} (K={wl.K}, d={wl.d}), "
+              f"{s_iter_sample:.3f} s/iter, scaled x{wl.N / n:.2f} to N={wl.N}")
+    return s_iter_full, sample, kind, threads
+
+
+def run_reference(args, wl):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    op, kind = load_reference_op()
+    # each step: one EM iteration; on a sample of the workload if the full size is slow
+    n = min(wl.N, 4096)
+    X, mu, var, lp = make_workload(wl, N=n)
+    t0 = time.perf_counter()
+    op(X, mu, var, lp)
+    per_point = (time.perf_counter() - t0) / n
+    budget_total = 150.0
+    per_step = budget_total / max(1, args.steps + args.warmup)
+    n = int(min(wl.N, max(1024, per_step / max(per_point, 1e-12))))
+    X, mu, var, lp = make_workload(wl, N=n)
+    for _ in range(args.warmup):
+        mu, var, lp, ln = op(X, mu, var, lp)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        mu, var, lp, ln = op(X, mu, var, lp)
+    dt = time.perf_counter() - t0
+    s_iter = dt / args.steps * wl.N / n
+    value = 1.0 / s_iter
+    sample = (f"{args.steps} iterations at N={n} of workload {wl.name}, scaled x{wl.N / n:.2f} "
+              f"to N={wl.N} (cost linear in N)")
+    line = {
+        "impl": "reference", "metric": f"EM iterations/s ({wl.name}: N={wl.N}, K={wl.K}, d={wl.d})",
+        "value": value, "unit": "iter/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": s_iter * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": wl.name, "N": wl.N, "K": wl.K, "d": wl.d, "device": "host cpu"},
+        "cpu_baseline": {"value": value, "unit": "iter/s", "cores": threads, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "iter/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------ our arm
+def profile_dominant(C, X, points, mu, var, lp, ws, reps=5):
+    """CUDA-event duration of every launch of one em_stats call (avg over reps)."""
+    import ctypes
+    from flashgmm_b200 import _lib
+    lib = _lib.load()
+    N, d = X.shape
+    K = mu.shape[0]
+    nmax = 16
+    acc = {}
+    for _ in range(reps):
+        ms = (ctypes.c_float * nmax)()
+        names = (ctypes.c_char_p * nmax)()
+        _lib.check(lib.fgmm_em_stats_profiled(
+            X.data_ptr(), points.data_ptr() if points is not None else None, N, d, mu.data_ptr(),
+            var.data_ptr(), lp.data_ptr(), K, ws.stats.data_ptr(), ws.ln.data_ptr(),
+            ws.ws.data_ptr(), ws.ws.numel(), torch.cuda.current_stream().cuda_stream, ms, names,
+            nmax))
+        for i in range(nmax):
+            if names[i] is None:
+                break
+            acc.setdefault(names[i].decode(), []).append(ms[i])
+    return {k: sum(v) / len(v) for k, v in acc.items()}
+
+
+def run_ours(args, wl):
+    ws_n, rank, local = dist_env()
+    if ws_n > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from flashgmm_b200 import _lib
+    from flashgmm_b200 import flash_gmm_native as C
+    lib = _lib.load()
+
+    # each rank: a full workload-sized shard of an (n_gpus x N)-point data set
+    n_total = wl.N * ws_n
+    X, mu, var, lp = make_workload(wl, N=n_total, rows=(rank * wl.N, (rank + 1) * wl.N))
+    X, mu0, var0, lp0 = (t.to(dev).contiguous() for t in (X, mu, var, lp))
+    N, d, K = wl.N, wl.d, wl.K
+    points = C.prepare_points(X, K)
+    ws = C.StatsWorkspace(N, d, K, dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    mu, var, lp = mu0.clone(), var0.clone(), lp0.clone()
+
+    def step():
+        nonlocal mu, var, lp
+        stats, _ = C.em_stats(X, mu, var, lp, points=points, workspace=ws)
+        if ws_n > 1:
+            dist.all_reduce(stats)
+        mu, var, lp = C.em_update(stats, n_total, K, d)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    clocks = ClockSampler(gpu_id(dev)).start() if rank == 0 else None
+    if ws_n > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush.zero_()  # untimed: evict X / operands from L2 between iterations
+        ev[i][0].record()
+        step()
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    if ws_n > 1:
+        dist.barrier()
+    clk = clocks.stop() if clocks else None
+    total_ms = sum(a.elapsed_time(b) for a, b in ev)
+    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+    if ws_n > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = t.item()
+    ms_per_step = total_ms / args.steps
+    value = ws_n * 1000.0 / ms_per_step  # workload-sized iterations per second, all ranks
+
+    # dominant kernel: per-launch CUDA-event durations of the em_stats sequence
+    prof = profile_dominant(C, X, points, mu, var, lp, ws)
+    dom = max(prof, key=prof.get)
+    pk = peaks()
+    tf32_eff = pk["bf16_tflops"] / 2.0 / 3.0  # 3xTF32: three TF32 products per fp32 product
+    flops, nbytes = algorithmic(wl, N)
+    # the dominant kernel's share of the algorithmic work (pass 1: 4NKd, pass 2: 8NKd)
+    if "pass1" in dom:
+        f_dom = flops / 3.0
+    elif "pass2" in dom:
+        f_dom = flops * 2.0 / 3.0
+    else:
+        f_dom = flops
+    achieved = f_dom / (prof[dom] * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": tf32_eff,
+                "unit": "TFLOP/s", "frac": achieved / tf32_eff, "traffic": None,
+                "kernel_ms": prof[dom], "launch_ms": prof,
+                "peak_note": (f"3xTF32 effective = {pk['source']} bf16 {pk['bf16_tflops']:.0f} TF/s"
+                              " / 2 (tf32) / 3 (products)"),
+                "iteration_frac": (flops / (ms_per_step * 1e-3) / 1e12) / tf32_eff,
+                "algorithmic": {"flops_per_iter": flops, "bytes_per_iter": nbytes}}
+
+    launches = lib.fgmm_em_stats_launches(N, d, K) + 1
+    e2e = None
+    cpu = None
+    if ws_n == 1 and not args.no_e2e:
+        e2e = run_e2e(wl, dev, args)
+    if rank == 0 and ws_n == 1 and not args.no_cpu_baseline:
+        s_full, sample, kind, threads = cpu_time_per_iter(wl)
+        cpu = {"value": 1.0 / s_full, "unit": "iter/s", "cores": threads, "kind": kind,
+               "sample": sample}
+    if rank == 0:
+        line = {
+            "metric": f"EM iterations/s ({wl.name}: N={wl.N}, K={wl.K}, d={wl.d})",
+            "value": value, "unit": "iter/s", "n_gpus": ws_n, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": wl.name, "N_per_gpu": N, "K": K, "d": d,
+                       "N_total": n_total, "parallelism": f"dp{ws_n}" if ws_n > 1 else "single",
+                       "family": {1: "simt", 2: "tcgen05"}.get(C.family_for(N, d, K), "?"),
+                       "l2": "flushed between timed iterations (256 MB write, untimed)"},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+            "gpu_launches": launches * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    if ws_n > 1:
+        dist.destroy_process_group()
+
+
+def run_e2e(wl, dev, args):
+    """Whole fits through the public API from pinned host memory: H2D of X and the
+    initial parameters, FIT_ITERS EM iterations, D2H of the fitted parameters."""
+    from flashgmm_b200.native_wrapper import NativeFlashGMM
+    X, mu, var, lp = make_workload(wl)
+    Xh = X.pin_memory()
+    init_h = [t.pin_memory() for t in (mu, var, lp)]
+    m = NativeFlashGMM(K=wl.K, d=wl.d, max_iter=FIT_ITERS, tol=0.0, device=dev)
+
+    def one():
+        Xd = Xh.to(dev, non_blocking=True)
+        init = [t.to(dev, non_blocking=True) for t in init_h]
+        m.fit(Xd, init=init)
+        return [m.mu.cpu(), m.var.cpu(), m.log_pi.cpu()]
+
+    one()
+    reps = 3
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        out = one()
+    dt = (time.perf_counter() - t0) / reps
+    h2d = Xh.numel() * 4 + sum(t.numel() * 4 for t in init_h)
+    d2h = sum(t.numel() * 4 for t in out) + 8 * FIT_ITERS
+    return {"value": FIT_ITERS / dt, "unit": "iter/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
+            "step": f"NativeFlashGMM.fit of {FIT_ITERS} iterations from pinned host X (wall clock)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="flashgmm", choices=["flashgmm", "reference"])
+    ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, wl)
+    else:
+        run_ours(args, wl)
+
+
+if __name__ == "__main__":
+    main()

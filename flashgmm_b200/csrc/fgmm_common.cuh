@@ -1,0 +1,93 @@
+// Shared helpers for the flashgmm_b200 CUDA library (host + device).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stddef.h>
+#include <string>
+
+#include "../../include/flashgmm_b200.h"
+
+namespace fgmm {
+
+constexpr double kLog2Pi = 1.8378770664093453;
+
+// Per-host-thread error message behind fgmm_last_error().
+void set_error(const std::string &msg);
+int fail(int code, const std::string &msg);
+int cuda_fail(cudaError_t e, const char *what);
+
+#define FGMM_CUDA_TRY(expr)                                   \
+  do {                                                        \
+    cudaError_t _e = (expr);                                  \
+    if (_e != cudaSuccess) return ::fgmm::cuda_fail(_e, #expr); \
+  } while (0)
+
+#define FGMM_LAUNCH_CHECK(what)                               \
+  do {                                                        \
+    cudaError_t _e = cudaGetLastError();                      \
+    if (_e != cudaSuccess) return ::fgmm::cuda_fail(_e, what); \
+  } while (0)
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Bump allocator over a caller-provided workspace.
+struct Carve {
+  char *base;
+  size_t off = 0;
+  explicit Carve(void *p) : base(static_cast<char *>(p)) {}
+  template <class T> T *take(size_t count) {
+    off = align_up(off, 256);
+    T *p = base ? reinterpret_cast<T *>(base + off) : nullptr;
+    off += count * sizeof(T);
+    return p;
+  }
+  size_t bytes() const { return align_up(off, 256); }
+};
+
+int num_sms();
+
+// Optional per-launch event recording (active only inside fgmm_em_stats_profiled).
+struct PhaseTimer {
+  static constexpr int kMax = 16;
+  cudaEvent_t ev[kMax + 1];
+  const char *name[kMax];
+  int n = 0;
+};
+PhaseTimer *&phase_timer();
+// Record the end of the launch just issued on `st` (no-op when not profiling).
+inline void mark(cudaStream_t st, const char *name) {
+  PhaseTimer *t = phase_timer();
+  if (t && t->n < PhaseTimer::kMax) {
+    t->name[t->n] = name;
+    cudaEventRecord(t->ev[++t->n], st);
+  }
+}
+int simt_launches();
+int tc_launches(int64_t N, int d, int K);
+
+// ---- SIMT family (fgmm_simt.cu) ----
+size_t simt_workspace_bytes(int64_t N, int d, int K);
+int simt_em_stats(const float *X, int64_t N, int d, const float *mu, const float *var,
+                  const float *log_pi, int K, double *stats, float *log_norm,
+                  void *ws, cudaStream_t stream);
+
+// ---- tcgen05 family (fgmm_tc.cu) ----
+bool tc_supported(int64_t N, int d, int K);
+size_t tc_points_bytes(int64_t N, int d);
+size_t tc_workspace_bytes(int64_t N, int d, int K);
+int tc_prepare_points(const float *X, int64_t N, int d, void *points, cudaStream_t stream);
+int tc_em_stats(const float *X, const void *points, int64_t N, int d, const float *mu,
+                const float *var, const float *log_pi, int K, double *stats,
+                float *log_norm, void *ws, cudaStream_t stream);
+
+// ---- shared epilogue kernels (fgmm_update.cu) ----
+// Sums per-block fp32 partials [slots][K][2d+1] and per-block log-normalizer
+// sums into the packed fp64 stats vector.
+int reduce_partials(const float *partials, int slots, int K, int d,
+                    const double *ln_partials, int ln_slots, double *stats,
+                    cudaStream_t stream);
+int em_update(const double *stats, double n_total, int K, int d, float *new_mu,
+              float *new_var, float *new_log_pi, cudaStream_t stream);
+
+}  // namespace fgmm

@@ -1,0 +1,116 @@
+/*
+ * flashgmm_b200.h -- C ABI of the B200 (sm_100a) fused diagonal-covariance EM
+ * iteration.  Plain pointers and sizes only; every pointer argument named
+ * X / mu / var / log_pi / new_* / stats / log_normalizer / gamma / workspace /
+ * points is DEVICE memory on the current CUDA device, and `stream` is a
+ * cudaStream_t (NULL = legacy default stream).  All calls are asynchronous with
+ * respect to the host unless stated otherwise.
+ *
+ * Layouts: X[N][d], mu[K][d], var[K][d], gamma[N][K] are row-major fp32;
+ * log_pi[K], log_normalizer[N] fp32.  `stats` is the packed fp64 sufficient
+ * statistics vector of length fgmm_stats_len(K, d):
+ *     [ n_k (K) | s_k (K*d) | sq_k (K*d) | sum_n log_normalizer_n (1) ]
+ * which is what a multi-GPU caller sums across ranks between fgmm_em_stats and
+ * fgmm_em_update.
+ *
+ * Return value: FGMM_OK (0) or an FGMM_ERR_* code; fgmm_last_error() gives the
+ * message of the last failure on the calling host thread.
+ */
+#ifndef FLASHGMM_B200_H_
+#define FLASHGMM_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FGMM_OK 0
+#define FGMM_ERR_INVALID 1      /* bad shape / null pointer / misaligned pointer */
+#define FGMM_ERR_UNSUPPORTED 2  /* shape outside what the kernels handle (d > 256) */
+#define FGMM_ERR_WORKSPACE 3    /* workspace smaller than the *_bytes query */
+#define FGMM_ERR_CUDA 4         /* a CUDA runtime call or kernel launch failed */
+
+/* Kernel families fgmm_em_stats can run. */
+#define FGMM_FAMILY_AUTO 0      /* tcgen05 tensor-core kernels where the shape allows, else SIMT */
+#define FGMM_FAMILY_SIMT 1      /* force the generic fp32 CUDA-core kernels */
+#define FGMM_FAMILY_TC 2        /* require the tcgen05 kernels (error if the shape is outside them) */
+
+const char *fgmm_last_error(void);
+int fgmm_version(void);
+
+/* Select the kernel family used by subsequent fgmm_em_stats / fgmm_em_fused
+ * calls in this process (default FGMM_FAMILY_AUTO).  Returns the previous value. */
+int fgmm_set_family(int family);
+/* Which family fgmm_em_stats would run for this shape under the current setting
+ * (FGMM_FAMILY_SIMT or FGMM_FAMILY_TC), or -1 if the shape is unsupported. */
+int fgmm_family_for(int64_t N, int32_t d, int32_t K);
+
+/* Length (in doubles) of the packed statistics vector: K*(2d+1)+1. */
+int64_t fgmm_stats_len(int32_t K, int32_t d);
+
+/* Bytes of the "prepared points" buffer for X[N][d]: the per-point tensor-core
+ * operand rows [x^2 | x] split into tf32 hi/lo parts.  X is constant over an EM
+ * fit, so a caller may prepare once and pass `points` to every fgmm_em_stats.
+ * Returns 0 when the shape runs on the SIMT family (no preparation needed). */
+size_t fgmm_points_bytes(int64_t N, int32_t d, int32_t K);
+int fgmm_prepare_points(const float *X, int64_t N, int32_t d, int32_t K,
+                        void *points, size_t points_bytes, void *stream);
+
+/* Scratch needed by fgmm_em_stats (parameter operands, per-block partial
+ * statistics and log-sum-exp partials).  256-byte aligned pointer required. */
+size_t fgmm_em_stats_workspace_bytes(int64_t N, int32_t d, int32_t K);
+
+/* Pass 1 (online log-sum-exp -> log_normalizer[N]) and Pass 2 (responsibilities
+ * recomputed on chip, accumulated into n_k, s_k = gamma^T X, sq_k = gamma^T X^2)
+ * over the N local points.  Writes `stats` (fp64, see above) and
+ * `log_normalizer`.  `points` may be NULL, in which case the tensor-core family
+ * prepares the operands inside `workspace` (which must then be at least
+ * fgmm_em_fused_workspace_bytes).
+ * Replaces the first three launches of flash_em_fused_cuda
+ * (reference flash_gmm/csrc/flash_gmm_cuda.cu:418-493: precompute_params_kernel,
+ * flash_log_normalizer_v2_kernel, flash_accumulate_stats_v2_kernel). */
+int fgmm_em_stats(const float *X, const void *points, int64_t N, int32_t d,
+                  const float *mu, const float *var, const float *log_pi, int32_t K,
+                  double *stats, float *log_normalizer,
+                  void *workspace, size_t workspace_bytes, void *stream);
+
+/* M-step from (globally summed) statistics: mu = s/max(n,1e-8),
+ * var = max(sq/n - mu^2, 1e-6), log_pi = log(max(n/n_total, 1e-8)).
+ * Replaces update_params_kernel (reference flash_gmm/csrc/flash_gmm_cuda.cu:298-322,
+ * launched at :496-501) with the same floors as flash_gmm/csrc/flash_gmm_cpu.cpp:270-284. */
+int fgmm_em_update(const double *stats, double n_total, int32_t K, int32_t d,
+                   float *new_mu, float *new_var, float *new_log_pi, void *stream);
+
+/* One fused EM iteration on one device: stats + update.  The drop-in for the
+ * reference's op `flash_em_fused(X, mu, var, log_pi, BN, BK)`
+ * (flash_gmm/csrc/binding.cpp:62-76 dispatching to flash_em_fused_cuda,
+ * flash_gmm/csrc/flash_gmm_cuda.cu:402-504).  The reference's BN/BK tile hints
+ * have no counterpart: tile shapes are fixed by the kernels. */
+size_t fgmm_em_fused_workspace_bytes(int64_t N, int32_t d, int32_t K);
+int fgmm_em_fused(const float *X, int64_t N, int32_t d,
+                  const float *mu, const float *var, const float *log_pi, int32_t K,
+                  float *new_mu, float *new_var, float *new_log_pi, float *log_normalizer,
+                  void *workspace, size_t workspace_bytes, void *stream);
+
+/* Number of kernel launches one fgmm_em_stats call makes for this shape
+ * (fgmm_em_update adds one more). */
+int fgmm_em_stats_launches(int64_t N, int32_t d, int32_t K);
+
+/* Profiling variant of fgmm_em_stats: identical launches, with a CUDA event
+ * recorded on `stream` before the first and after every launch.  Synchronises
+ * the stream, then writes the duration (ms) of each launch into
+ * launch_ms[0 .. min(n, launches)-1] and, if names != NULL, a static name
+ * string per launch.  Returns the status of the wrapped call.  Has no
+ * counterpart in the reference (its launcher exposes no timing). */
+int fgmm_em_stats_profiled(const float *X, const void *points, int64_t N, int32_t d,
+                           const float *mu, const float *var, const float *log_pi, int32_t K,
+                           double *stats, float *log_normalizer,
+                           void *workspace, size_t workspace_bytes, void *stream,
+                           float *launch_ms, const char **names, int32_t n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FLASHGMM_B200_H_ */
