@@ -167,6 +167,8 @@ int fgmm_em_fused(const float *X, int64_t N, int32_t d, const float *mu, const f
   return fgmm_em_update(stats, (double)N, K, d, new_mu, new_var, new_log_pi, stream);
 }
 
+int fgmm_device_error(int reset) { return tc_device_error(reset != 0); }
+
 int fgmm_em_stats_launches(int64_t N, int32_t d, int32_t K) {
   const int fam = resolve_family(N, d, K);
   if (fam == FGMM_FAMILY_SIMT) return simt_launches();

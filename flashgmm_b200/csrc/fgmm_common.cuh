@@ -77,14 +77,16 @@ bool tc_supported(int64_t N, int d, int K);
 size_t tc_points_bytes(int64_t N, int d);
 size_t tc_workspace_bytes(int64_t N, int d, int K);
 int tc_prepare_points(const float *X, int64_t N, int d, void *points, cudaStream_t stream);
+// Code of the first bounded-wait failure recorded by a tensor-core kernel (0 = none).
+int tc_device_error(bool reset);
 int tc_em_stats(const float *X, const void *points, int64_t N, int d, const float *mu,
                 const float *var, const float *log_pi, int K, double *stats,
                 float *log_norm, void *ws, cudaStream_t stream);
 
 // ---- shared epilogue kernels (fgmm_update.cu) ----
-// Sums per-block fp32 partials [slots][K][2d+1] and per-block log-normalizer
-// sums into the packed fp64 stats vector.
-int reduce_partials(const float *partials, int slots, int K, int d,
+// Sums per-block fp32 partials [slots][K][W] (rows [s (ds) | sq (ds) | n ...]) and
+// per-block log-normalizer sums into the packed fp64 stats vector (one launch).
+int reduce_partials(const float *partials, int slots, int K, int d, int ds, int W,
                     const double *ln_partials, int ln_slots, double *stats,
                     cudaStream_t stream);
 int em_update(const double *stats, double n_total, int K, int d, float *new_mu,

@@ -268,7 +268,7 @@ int simt_launch(const float *X, int64_t N, int d, int K, const SimtWs &w, float 
 
 }  // namespace
 
-int simt_launches() { return 5; }
+int simt_launches() { return 4; }
 
 size_t simt_workspace_bytes(int64_t N, int d, int K) { return simt_layout(nullptr, N, d, K).bytes; }
 
@@ -290,7 +290,7 @@ int simt_em_stats(const float *X, int64_t N, int d, const float *mu, const float
     default: rc = simt_launch<8>(X, N, d, K, w, log_norm, st); break;
   }
   if (rc != FGMM_OK) return rc;
-  return reduce_partials(w.partial, w.slots, K, d, w.ln_part, w.p1_blocks, stats, st);
+  return reduce_partials(w.partial, w.slots, K, d, d, 2 * d + 1, w.ln_part, w.p1_blocks, stats, st);
 }
 
 }  // namespace fgmm

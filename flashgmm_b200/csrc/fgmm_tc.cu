@@ -1,15 +1,845 @@
-// tcgen05 tensor-core family (placeholder until the kernels land).
+// tcgen05 tensor-core family of the fused EM statistics kernels (sm_100a).
+//
+// Both passes evaluate the Mahalanobis term through the expansion
+//   sum_j (x_j - mu_kj)^2 / var_kj = sum_j x_j^2 iv_kj - 2 sum_j x_j mu_kj iv_kj + sum_j mu_kj^2 iv_kj
+// as one GEMM per (point tile, component tile):
+//   acc[n,k] = P[n,:] . Q[k,:],   P[n] = [x^2 | x],  Q[k] = [iv | -2 mu iv]
+// with the constant folded into cst2_k = log2(e) (log_pi - 1/2 (d log 2pi + sum log var + sum mu^2 iv)),
+// so that log2-likelihood = cst2_k - (log2(e)/2) acc.  The GEMM runs in 3xTF32: every
+// operand is split v = hi + lo with hi, lo tf32, and acc += lo_P.hi_Q + hi_P.lo_Q + hi_P.hi_Q.
+// (Reference: the direct form in flash_gmm/csrc/flash_gmm_cuda.cu:135-156 and
+// flash_gmm/csrc/flash_gmm_cpu.cpp:30-45.)
+//
+// Pass 1 (log-normalizer): persistent CTAs over (point tile, component group) units;
+//   the accumulator lives in TMEM and eight epilogue warps run the online log-sum-exp of
+//   flash_gmm/csrc/flash_gmm_cuda.cu:145-155 in base 2, writing one (max, sum) partial
+//   per point and component group.
+// Pass 2 (statistics): CTA (component tile ct, slot) walks a contiguous range of point
+//   tiles.  Per tile: the distance GEMM again -> gamma = 2^(l2 - ln2) computed by the
+//   epilogue from TMEM and stored to shared memory (rounded to tf32) -> a second GEMM
+//   S[k, f] = sum_n gamma[n,k] F[n,f],  F[n] = [x^2 | x] (hi + lo: 2 products), and
+//   n_k = sum_n gamma[n,k] on the CUDA cores from the same rounded weights.  S is
+//   restarted every tile and added (fp32, round-to-nearest) into one partial row per
+//   CTA; the partials are reduced in fp64 afterwards: deterministic, no atomics
+//   between CTAs.  (Reference: flash_accumulate_stats_v2_kernel,
+//   flash_gmm/csrc/flash_gmm_cuda.cu:179-292, which accumulates with global atomics.)
+//
+// Warp roles (320 threads): warp 0 issues TMA loads, warp 1 owns TMEM and issues
+// tcgen05.mma (one thread), warps 2-9 are the epilogue: warp w reads TMEM lanes
+// 32*(w%4) .. +31, and warps w and w+4 split the 128 columns of a tile.  No cluster
+// multicast anywhere.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+
 #include "fgmm_common.cuh"
+#include "sm100_ptx.cuh"
+
 namespace fgmm {
-int tc_launches(int64_t, int, int) { return 0; }
-bool tc_supported(int64_t, int, int) { return false; }
-size_t tc_points_bytes(int64_t, int) { return 0; }
-size_t tc_workspace_bytes(int64_t, int, int) { return 0; }
-int tc_prepare_points(const float *, int64_t, int, void *, cudaStream_t) {
-  return fail(FGMM_ERR_UNSUPPORTED, "tcgen05 family not built");
+using namespace ptx;
+
+namespace {
+
+constexpr int BM = 128;                       // points per tile
+constexpr int NC = 128;                       // components per tile
+constexpr int KC = 32;                        // fp32 elements per K chunk (one 128-byte row)
+constexpr int kEpiWarps = 8;                  // two warps per TMEM lane quarter
+constexpr int kThreads = 64 + 32 * kEpiWarps; // warp 0 TMA, warp 1 MMA, warps 2.. epilogue
+constexpr int kEpiThreads = 32 * kEpiWarps;
+constexpr int kHalf = 64;                     // columns of a tile owned by one epilogue warp
+constexpr int kStages1 = 3;
+constexpr int kStages2 = 2;
+constexpr int kTileBytes = BM * KC * 4;       // 16 KB: 128 rows x 128 B
+constexpr int kStageBytes = 4 * kTileBytes;   // 64 KB
+constexpr int kSubBytes = 32 * KC * 4;        // 4 KB: 32 rows x 128 B
+constexpr int kGammaBytes = NC * BM * 4;      // 64 KB
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr int kMaxDp = 128;                   // d <= 128 runs here
+
+// Points buffer: P_hi and P_lo, each [Npad][2 dp] fp32 with Npad = N rounded up to a
+// whole 128-row tile (rows >= N are zero), so no TMA box ever leaves the tensor.
+inline int dp_of(int d) { return (d + KC - 1) / KC * KC; }
+inline int64_t npad_of(int64_t N) { return cdiv(N, BM) * BM; }
+inline size_t points_half_floats(int64_t N, int d) {
+  return align_up((size_t)npad_of(N) * 2 * dp_of(d), 256);
 }
-int tc_em_stats(const float *, const void *, int64_t, int, const float *, const float *,
-                const float *, int, double *, float *, void *, cudaStream_t) {
-  return fail(FGMM_ERR_UNSUPPORTED, "tcgen05 family not built");
+
+__device__ __forceinline__ uint8_t *align1024(uint8_t *p) {
+  uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  return reinterpret_cast<uint8_t *>((a + 1023) & ~uintptr_t(1023));
 }
+
+// --------------------------------------------------------------------------- prep
+// P[n] = [x^2 (dp) | x (dp)] split into tf32 hi/lo (zero for j >= d and rows n >= N).
+__global__ void tc_prep_points_kernel(const float *__restrict__ X, int64_t N, int64_t Npad, int d,
+                                      int dp, float *__restrict__ phi, float *__restrict__ plo) {
+  const int KA = 2 * dp;
+  const int64_t total = Npad * dp;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = i / dp;
+    const int j = (int)(i - n * dp);
+    const float x = (j < d && n < N) ? __ldg(X + n * d + j) : 0.0f;
+    const float x2 = x * x;
+    const float x2h = to_tf32(x2), xh = to_tf32(x);
+    phi[n * KA + j] = x2h;
+    plo[n * KA + j] = to_tf32(x2 - x2h);
+    phi[n * KA + dp + j] = xh;
+    plo[n * KA + dp + j] = to_tf32(x - xh);
+  }
+}
+
+// Q[k] = [iv (dp) | -2 mu iv (dp)] (hi/lo of the fp64 value), cst2[k]; rows k >= K are
+// zero with cst2 = -inf (padding components never receive responsibility).
+__global__ void tc_prep_params_kernel(const float *__restrict__ mu, const float *__restrict__ var,
+                                      const float *__restrict__ log_pi, int K, int d, int dp,
+                                      float *__restrict__ qhi, float *__restrict__ qlo,
+                                      float *__restrict__ cst2) {
+  const int k = blockIdx.x;
+  const int KA = 2 * dp;
+  __shared__ double red[8];
+  double acc = 0.0;  // sum_j (log var + mu^2 / var)
+  for (int j = threadIdx.x; j < dp; j += blockDim.x) {
+    double iv = 0.0, b = 0.0;
+    if (k < K && j < d) {
+      const double v = var[(int64_t)k * d + j];
+      const double m = mu[(int64_t)k * d + j];
+      iv = 1.0 / v;
+      b = -2.0 * m * iv;
+      acc += log(v) + m * m * iv;
+    }
+    const float ivh = to_tf32((float)iv), bh = to_tf32((float)b);
+    qhi[(int64_t)k * KA + j] = ivh;
+    qlo[(int64_t)k * KA + j] = to_tf32((float)(iv - (double)ivh));
+    qhi[(int64_t)k * KA + dp + j] = bh;
+    qlo[(int64_t)k * KA + dp + j] = to_tf32((float)(b - (double)bh));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+    cst2[k] = (k < K) ? (float)(1.4426950408889634 *
+                                ((double)log_pi[k] - 0.5 * (d * kLog2Pi + t)))
+                      : -INFINITY;
+  }
+}
+
+// ------------------------------------------------------------- shared pieces
+// Named barrier 1 across the epilogue warps that also ANDs a flag, so every epilogue
+// warp takes the same early-exit decision (no warp is left waiting at a barrier).
+__device__ __forceinline__ bool epi_sync_and(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "n"(kEpiThreads)
+      : "memory");
+  return r != 0;
+}
+
+// The distance GEMM is accumulated per 32-column K group (one staged chunk): each group
+// goes into a fresh TMEM buffer, the 8 small cross products (lo.hi, hi.lo) first and the
+// 4 hi.hi products last, and the epilogue adds the groups in fp32 registers.
+// Tensor-memory accumulation does not round to nearest, so one long accumulation at the
+// magnitude of the expanded form (|x|^2/var ~ thousands) drifts by ~1e-2; short groups
+// with the small terms summed first, added on the CUDA cores, match a direct fp32
+// evaluation of the Mahalanobis sum.
+
+// MMA side: one staged 32-column chunk = one group, rotating over NB TMEM buffers.
+template <int NB>
+__device__ __forceinline__ bool issue_dist_chunk(uint32_t base, uint32_t tmem, uint32_t &gcount,
+                                                 uint32_t tfull0, uint32_t tempty0) {
+  constexpr uint32_t idesc = idesc_tf32(BM, NC, 0, 0);
+  const uint32_t buf = gcount % NB, use = gcount / NB;
+  if (!mbar_wait(tempty0 + 8u * buf, (use & 1u) ^ 1u, kErrWaitTmemEmpty)) return false;
+  tc_fence_after();
+  const uint32_t d = tmem + buf * NC;
+#pragma unroll
+  for (int kk = 0; kk < KC / 8; ++kk) {
+    const uint64_t ah = sdesc_sw128(base + kk * 32, 16, 1024);
+    const uint64_t al = sdesc_sw128(base + kTileBytes + kk * 32, 16, 1024);
+    const uint64_t bh = sdesc_sw128(base + 2 * kTileBytes + kk * 32, 16, 1024);
+    const uint64_t bl = sdesc_sw128(base + 3 * kTileBytes + kk * 32, 16, 1024);
+    mma_tf32(d, al, bh, idesc, kk != 0 ? 1u : 0u);
+    mma_tf32(d, ah, bl, idesc, 1u);
+  }
+#pragma unroll
+  for (int kk = 0; kk < KC / 8; ++kk) {
+    const uint64_t ah = sdesc_sw128(base + kk * 32, 16, 1024);
+    const uint64_t bh = sdesc_sw128(base + 2 * kTileBytes + kk * 32, 16, 1024);
+    mma_tf32(d, ah, bh, idesc, 1u);
+  }
+  mma_commit(tfull0 + 8u * buf);
+  ++gcount;
+  return true;
+}
+
+// Epilogue side: add the next group buffer into acc (this warp's 32 rows, its 64 columns;
+// lane_tmem already points at the warp's lane quarter and column half).
+template <int NB, bool kFirst>
+__device__ __forceinline__ bool drain_group(uint32_t lane_tmem, uint32_t &gcount, uint32_t tfull0,
+                                            uint32_t tempty0, float (&acc)[kHalf], int lane) {
+  const uint32_t buf = gcount % NB, use = gcount / NB;
+  if (!__all_sync(0xffffffffu, mbar_wait(tfull0 + 8u * buf, use & 1u, kErrWaitTmemFull)))
+    return false;
+  tc_fence_after();
+#pragma unroll
+  for (int h = 0; h < kHalf / 16; ++h) {
+    float v[16];
+    tmem_ld16(lane_tmem + buf * NC + h * 16, v);
+    tmem_wait_ld();
+#pragma unroll
+    for (int e = 0; e < 16; ++e) acc[h * 16 + e] = kFirst ? v[e] : acc[h * 16 + e] + v[e];
+  }
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(tempty0 + 8u * buf);
+  ++gcount;
+  return true;
+}
+
+// ------------------------------------------------------------------------- pass 1
+template <int NKC>
+__global__ void __launch_bounds__(kThreads, 1)
+tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ CUtensorMap tm_plo,
+                const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant__ CUtensorMap tm_qlo,
+                const float *__restrict__ cst2, int64_t N, int n_pt, int n_ct, int G, int tpg,
+                float *__restrict__ part_m, float *__restrict__ part_s) {
+  constexpr int S = kStages1;
+  constexpr int NB = 4;  // TMEM group buffers (4 x 128 columns)
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = align1024(smem_raw);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * kStageBytes);
+  // bars: full[S] empty[S] tfull[NB] tempty[NB] done
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 2 * NB + 1);
+  float2 *lse_x = reinterpret_cast<float2 *>(tmem_slot + 2);  // [128] half-row LSE exchange
+  const uint32_t bar0 = smem_u32(bars);
+  auto FULL = [&](int s) { return bar0 + 8u * s; };
+  auto EMPTY = [&](int s) { return bar0 + 8u * (S + s); };
+  const uint32_t TFULL0 = bar0 + 8u * (2 * S), TEMPTY0 = bar0 + 8u * (2 * S + NB);
+  const uint32_t DONE = bar0 + 8u * (2 * S + 2 * NB);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) { mbar_init(FULL(s), 1); mbar_init(EMPTY(s), 1); }
+    for (int b = 0; b < NB; ++b) {
+      mbar_init(TFULL0 + 8u * b, 1);
+      mbar_init(TEMPTY0 + 8u * b, kEpiWarps);
+    }
+    mbar_init(DONE, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int n_units = n_pt * G;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tm_phi); prefetch_tmap(&tm_plo); prefetch_tmap(&tm_qhi); prefetch_tmap(&tm_qlo);
+      int stage = 0;
+      uint32_t phase = 0, armed = 0, armed_par = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+        const int pt = u / G, g = u % G;
+        const int t1 = min(n_ct, (g + 1) * tpg);
+        for (int t = g * tpg; t < t1 && ok; ++t) {
+          for (int c = 0; c < NKC; ++c) {
+            if (!mbar_wait(EMPTY(stage), phase ^ 1, kErrWaitEmpty)) { ok = false; break; }
+            const uint32_t base = smem_u32(smem + stage * kStageBytes);
+            mbar_arrive_expect_tx(FULL(stage), kStageBytes);
+            tma_load_2d(base, &tm_phi, c * KC, pt * BM, FULL(stage));
+            tma_load_2d(base + kTileBytes, &tm_plo, c * KC, pt * BM, FULL(stage));
+            tma_load_2d(base + 2 * kTileBytes, &tm_qhi, c * KC, t * NC, FULL(stage));
+            tma_load_2d(base + 3 * kTileBytes, &tm_qlo, c * KC, t * NC, FULL(stage));
+            armed |= 1u << stage;
+            armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
+            if (++stage == S) { stage = 0; phase ^= 1; }
+          }
+        }
+      }
+      // never leave the CTA with bulk copies in flight
+      for (int s = 0; s < S; ++s)
+        if (armed & (1u << s)) mbar_wait(FULL(s), (armed_par >> s) & 1u, kErrWaitDrain);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, gcount = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+        const int g = u % G;
+        const int t1 = min(n_ct, (g + 1) * tpg);
+        for (int t = g * tpg; t < t1 && ok; ++t) {
+          for (int c = 0; c < NKC; ++c) {
+            if (!mbar_wait(FULL(stage), phase, kErrWaitFull)) { ok = false; break; }
+            tc_fence_after();
+            if (!issue_dist_chunk<NB>(smem_u32(smem + stage * kStageBytes), tmem, gcount, TFULL0,
+                                      TEMPTY0)) { ok = false; break; }
+            mma_commit(EMPTY(stage));
+            if (++stage == S) { stage = 0; phase ^= 1; }
+          }
+        }
+      }
+      mma_commit(DONE);
+      mbar_wait(DONE, 0, kErrWaitDrain);
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3, half = (warp - 2) >> 2;
+    const int row = q * 32 + lane;
+    const uint32_t lane_tmem = tmem + ((uint32_t)(q * 32) << 16) + half * kHalf;
+    uint32_t gcount = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+      const int pt = u / G, g = u % G;
+      const int t1 = min(n_ct, (g + 1) * tpg);
+      float m = -INFINITY, s = 0.0f;
+      for (int t = g * tpg; t < t1 && ok; ++t) {
+        float acc[kHalf];
+        ok = drain_group<NB, true>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
+#pragma unroll 1
+        for (int grp = 1; grp < NKC && ok; ++grp)
+          ok = drain_group<NB, false>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
+        if (!ok) break;
+        const float *cp = cst2 + (int64_t)t * NC + half * kHalf;
+#pragma unroll
+        for (int j = 0; j < kHalf / 32; ++j) {
+          float cm = -INFINITY;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            acc[j * 32 + e] = fmaf(acc[j * 32 + e], -0.5f * kLog2e, __ldg(cp + j * 32 + e));
+            cm = fmaxf(cm, acc[j * 32 + e]);
+          }
+          const float mn = fmaxf(m, cm);
+          const float mr = (mn == -INFINITY) ? 0.0f : mn;
+          float a = s * ex2(m - mr);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) a += ex2(acc[j * 32 + e] - mr);
+          s = a;
+          m = mn;
+        }
+      }
+      // merge the two column halves of each row
+      if (half == 1) lse_x[row] = make_float2(m, s);
+      ok = epi_sync_and(ok);
+      if (half == 0) {
+        const float2 o = lse_x[row];
+        const float mn = fmaxf(m, o.x);
+        const float mr = (mn == -INFINITY) ? 0.0f : mn;
+        const float sm = s * ex2(m - mr) + o.y * ex2(o.x - mr);
+        const int64_t n = (int64_t)pt * BM + row;
+        if (ok && n < N) {
+          part_m[(int64_t)g * N + n] = mn;
+          part_s[(int64_t)g * N + n] = sm;
+        }
+      }
+      ok = epi_sync_and(ok);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------------- pass 2
+// Add (or, for the first tile j == 0, store) the TMEM statistics of tile j into the CTA's
+// partial row `dst` ([s (DP) | sq (DP) | n | pad]); warp half 0 takes the x^2 features
+// (-> sq), half 1 the x features (-> s).  dst == nullptr: padding component, no store.
+template <int NKC>
+__device__ __forceinline__ bool drain_stats(int j, uint32_t sfull, uint32_t sempty,
+                                            uint32_t stats_tmem, int half, int lane, float *dst) {
+  constexpr int DP = NKC * KC / 2;
+  if (!__all_sync(0xffffffffu, mbar_wait(sfull, j & 1, kErrWaitStatsDone))) return false;
+  tc_fence_after();
+#pragma unroll 1
+  for (int c = half * (NKC / 2); c < (half + 1) * (NKC / 2); ++c) {
+    float v[32];
+    tmem_ld32(stats_tmem + c * 32, v);
+    tmem_wait_ld();
+    if (dst) {
+      float *o = dst + (half == 0 ? DP + c * 32 : c * 32 - DP);
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) {
+        const float4 w = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+        if (j > 0) red_add_v4(o + e, w);  // same-thread store/reds to one address stay ordered
+        else *reinterpret_cast<float4 *>(o + e) = w;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(sempty);
+  return true;
+}
+
+// Partial statistics row (per CTA slot and component): [s (DP) | sq (DP) | n | pad],
+// stride 2 DP + 4.
+template <int NKC>
+__global__ void __launch_bounds__(kThreads, 1)
+tc_pass2_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ CUtensorMap tm_plo,
+                const __grid_constant__ CUtensorMap tm_phi32, const __grid_constant__ CUtensorMap tm_plo32,
+                const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant__ CUtensorMap tm_qlo,
+                const float *__restrict__ cst2, const float *__restrict__ part_m,
+                const float *__restrict__ part_s, int64_t N, int n_pt, int G, int S_slots, int K,
+                float *__restrict__ partial, float *__restrict__ ln_out,
+                double *__restrict__ ln_part) {
+  constexpr int S = kStages2;
+  constexpr int KA = NKC * KC;
+  constexpr int DP = KA / 2;
+  constexpr int PSTRIDE = 2 * DP + 4;
+  constexpr int NB = (512 - KA) / NC;       // TMEM group buffers for the distance GEMM
+  constexpr uint32_t kColStats = NB * NC;   // TMEM column of S[k, f]
+  static_assert(NB >= 2, "TMEM budget");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = align1024(smem_raw);
+  uint8_t *gamma = smem + S * kStageBytes;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(gamma + kGammaBytes);
+  // bars: full[S] empty[S] tfull[NB] tempty[NB] gfull gempty sfull sempty
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 2 * NB + 4);
+  double *lred = reinterpret_cast<double *>(bars + 2 * S + 2 * NB + 5);  // [kEpiWarps]
+  float *nk_x = reinterpret_cast<float *>(lred + kEpiWarps);              // [128]
+  float *cst_s = nk_x + NC;                                                // [128] cst2 of this tile
+  const uint32_t bar0 = smem_u32(bars);
+  auto FULL = [&](int s) { return bar0 + 8u * s; };
+  auto EMPTY = [&](int s) { return bar0 + 8u * (S + s); };
+  const uint32_t TFULL0 = bar0 + 8u * (2 * S), TEMPTY0 = bar0 + 8u * (2 * S + NB);
+  const uint32_t GFULL = bar0 + 8u * (2 * S + 2 * NB), GEMPTY = GFULL + 8;
+  const uint32_t SFULL = GFULL + 16, SEMPTY = GFULL + 24;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ct = blockIdx.x / S_slots, slot = blockIdx.x % S_slots;
+  const int p0 = (int)((int64_t)slot * n_pt / S_slots);
+  const int p1 = (int)((int64_t)(slot + 1) * n_pt / S_slots);
+  const int T = p1 - p0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) { mbar_init(FULL(s), 1); mbar_init(EMPTY(s), 1); }
+    for (int b = 0; b < NB; ++b) {
+      mbar_init(TFULL0 + 8u * b, 1);
+      mbar_init(TEMPTY0 + 8u * b, kEpiWarps);
+    }
+    mbar_init(GFULL, kEpiWarps); mbar_init(GEMPTY, 1);
+    mbar_init(SFULL, 1); mbar_init(SEMPTY, kEpiWarps);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  if (threadIdx.x >= 64 && threadIdx.x < 64 + NC)
+    cst_s[threadIdx.x - 64] = cst2[(int64_t)ct * NC + threadIdx.x - 64];
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0 && T > 0) {
+      prefetch_tmap(&tm_phi); prefetch_tmap(&tm_plo); prefetch_tmap(&tm_phi32);
+      prefetch_tmap(&tm_plo32); prefetch_tmap(&tm_qhi); prefetch_tmap(&tm_qlo);
+      int stage = 0;
+      uint32_t phase = 0, armed = 0, armed_par = 0;
+      bool ok = true;
+      auto acquire = [&]() -> uint32_t {
+        if (!mbar_wait(EMPTY(stage), phase ^ 1, kErrWaitEmpty)) { ok = false; return 0; }
+        return smem_u32(smem + stage * kStageBytes);
+      };
+      auto advance = [&]() {
+        armed |= 1u << stage;
+        armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
+        if (++stage == S) { stage = 0; phase ^= 1; }
+      };
+      auto load_dist = [&](int pt) {
+        for (int c = 0; c < NKC && ok; ++c) {
+          const uint32_t base = acquire();
+          if (!ok) return;
+          mbar_arrive_expect_tx(FULL(stage), kStageBytes);
+          tma_load_2d(base, &tm_phi, c * KC, pt * BM, FULL(stage));
+          tma_load_2d(base + kTileBytes, &tm_plo, c * KC, pt * BM, FULL(stage));
+          tma_load_2d(base + 2 * kTileBytes, &tm_qhi, c * KC, ct * NC, FULL(stage));
+          tma_load_2d(base + 3 * kTileBytes, &tm_qlo, c * KC, ct * NC, FULL(stage));
+          advance();
+        }
+      };
+      auto load_stats = [&](int pt) {
+        for (int sub = 0; sub < BM / 32 && ok; ++sub) {
+          const uint32_t base = acquire();
+          if (!ok) return;
+          mbar_arrive_expect_tx(FULL(stage), 2 * NKC * kSubBytes);
+          for (int c = 0; c < NKC; ++c) {
+            tma_load_2d(base + c * kSubBytes, &tm_phi32, c * KC, pt * BM + sub * 32, FULL(stage));
+            tma_load_2d(base + (NKC + c) * kSubBytes, &tm_plo32, c * KC, pt * BM + sub * 32,
+                        FULL(stage));
+          }
+          advance();
+        }
+      };
+      load_dist(p0);
+      for (int i = 0; i < T && ok; ++i) {
+        if (i + 1 < T) load_dist(p0 + i + 1);
+        load_stats(p0 + i);
+      }
+      for (int s = 0; s < S; ++s)
+        if (armed & (1u << s)) mbar_wait(FULL(s), (armed_par >> s) & 1u, kErrWaitDrain);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && T > 0) {
+      constexpr uint32_t idesc_s = idesc_tf32(NC, KA, 1, 1);  // stats: MN-major A and B
+      const uint32_t gbase = smem_u32(gamma);
+      int stage = 0;
+      uint32_t phase = 0, gcount = 0;
+      bool ok = true;
+      auto issue_dist = [&]() {
+        for (int c = 0; c < NKC && ok; ++c) {
+          if (!mbar_wait(FULL(stage), phase, kErrWaitFull)) { ok = false; return; }
+          tc_fence_after();
+          if (!issue_dist_chunk<NB>(smem_u32(smem + stage * kStageBytes), tmem, gcount, TFULL0,
+                                    TEMPTY0)) { ok = false; return; }
+          mma_commit(EMPTY(stage));
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+      };
+      auto issue_stats = [&](int i) {
+        if (!mbar_wait(GFULL, i & 1, kErrWaitGammaFull)) { ok = false; return; }
+        if (i > 0 && !mbar_wait(SEMPTY, (i - 1) & 1, kErrWaitStatsDone)) { ok = false; return; }
+        tc_fence_after();
+        for (int sub = 0; sub < BM / 32; ++sub) {
+          if (!mbar_wait(FULL(stage), phase, kErrWaitFull)) { ok = false; return; }
+          tc_fence_after();
+          const uint32_t base = smem_u32(smem + stage * kStageBytes);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            // gamma^T: MN-major (components contiguous), 4-point atoms of 512 B, component
+            // atoms 16 KB apart; F: MN-major (features contiguous), 4 KB per 32 features.
+            const uint64_t a = sdesc(gbase + (sub * 4 + kk) * 1024, kGammaBytes / 4, 512, kSw128Base32);
+            const uint64_t fh = sdesc(base + kk * 1024, kSubBytes, 512, kSw128Base32);
+            const uint64_t fl = sdesc(base + NKC * kSubBytes + kk * 1024, kSubBytes, 512, kSw128Base32);
+            mma_tf32(tmem + kColStats, a, fl, idesc_s, (sub | kk) ? 1u : 0u);
+            mma_tf32(tmem + kColStats, a, fh, idesc_s, 1u);
+          }
+          mma_commit(EMPTY(stage));
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+        mma_commit(GEMPTY);
+        mma_commit(SFULL);
+      };
+      issue_dist();
+      for (int i = 0; i < T && ok; ++i) {
+        if (i + 1 < T) issue_dist();
+        if (!ok) break;
+        issue_stats(i);
+      }
+      if (!ok) {
+        mma_commit(SFULL);  // flush whatever was issued before giving up
+        mbar_wait(SFULL, 0, kErrWaitDrain);
+      }
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3, half = (warp - 2) >> 2;
+    const int row = q * 32 + lane;
+    const uint32_t lane_q = tmem + ((uint32_t)(q * 32) << 16);
+    const uint32_t lane_tmem = lane_q + half * kHalf;
+    const float *cp = cst_s + half * kHalf;
+    const int k = ct * NC + row;  // this thread's component row of the statistics
+    float *dst = partial + ((int64_t)slot * K + k) * PSTRIDE;
+    double lsum = 0.0;
+    float nk = 0.0f;
+    uint32_t gcount = 0;
+    bool ok = true;
+    for (int i = 0; i < T && ok; ++i) {
+      const int64_t n = (int64_t)(p0 + i) * BM + row;
+      const bool valid = n < N;
+      float ln2 = 0.0f;
+      if (valid) {  // merge the pass-1 (max, sum) partials of the component groups
+        float mx = -INFINITY;
+        for (int g = 0; g < G; ++g) mx = fmaxf(mx, __ldg(part_m + (int64_t)g * N + n));
+        float sm = 0.0f;
+        for (int g = 0; g < G; ++g)
+          sm += __ldg(part_s + (int64_t)g * N + n) * ex2(__ldg(part_m + (int64_t)g * N + n) - mx);
+        ln2 = mx + __log2f(sm);
+      }
+      float acc[kHalf];
+      ok = drain_group<NB, true>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
+#pragma unroll 1
+      for (int grp = 1; grp < NKC - 1 && ok; ++grp)
+        ok = drain_group<NB, false>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
+      ok = ok && __all_sync(0xffffffffu, mbar_wait(GEMPTY, (i & 1) ^ 1, kErrWaitGammaEmpty));
+      // The last K group is drained straight into gamma, 16 columns at a time: summed,
+      // turned into gamma = 2^(l2 - ln2) (tf32) and stored as the MN-major
+      // SWIZZLE_128B_BASE32B operand gamma^T (M = component, K = point): point p owns the
+      // 128-byte row p of each 32-component atom; its four 32-byte chunks (8 components
+      // each) sit at chunk index (c8 ^ (p % 4)); component atoms are 16 KB apart.  The two
+      // 16-byte halves of a chunk are stored in an order that differs between rows p and
+      // p+4, so a warp's stores hit every bank once per 128 bytes.
+      if (ok) {
+        const uint32_t buf = gcount % NB, use = gcount / NB;
+        ok = __all_sync(0xffffffffu, mbar_wait(TFULL0 + 8u * buf, use & 1u, kErrWaitTmemFull));
+        if (ok) {
+          tc_fence_after();
+          uint8_t *grow = gamma + row * 128;
+          const int flip = (row >> 2) & 1;
+#pragma unroll
+          for (int hh = 0; hh < kHalf / 16; ++hh) {
+            const int jj = hh >> 1;
+            float v[16];
+            tmem_ld16(lane_tmem + buf * NC + hh * 16, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c2 = 0; c2 < 2; ++c2) {
+              const int c8 = (hh & 1) * 2 + c2;
+              float gq[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const int col = hh * 16 + c2 * 8 + e;
+                const float l2 = fmaf(acc[col] + v[c2 * 8 + e], -0.5f * kLog2e, cp[col]);
+                gq[e] = valid ? to_tf32(ex2(l2 - ln2)) : 0.0f;
+              }
+              uint8_t *chunk = grow + (half * 2 + jj) * (kGammaBytes / 4) + ((c8 ^ (row & 3)) << 5);
+              const float4 lo4 = make_float4(gq[0], gq[1], gq[2], gq[3]);
+              const float4 hi4 = make_float4(gq[4], gq[5], gq[6], gq[7]);
+              *reinterpret_cast<float4 *>(chunk + (flip << 4)) = flip ? hi4 : lo4;
+              *reinterpret_cast<float4 *>(chunk + ((flip ^ 1) << 4)) = flip ? lo4 : hi4;
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(TEMPTY0 + 8u * buf);
+          ++gcount;
+          fence_proxy_async_smem();
+        }
+      }
+      ok = epi_sync_and(ok);  // every row of gamma is in place
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(GFULL);
+      {  // n_k: column `row` of gamma^T summed over this warp half's 64 points (the same
+         // tf32-rounded weights the statistics GEMM consumes)
+        const uint8_t *gcol = gamma + (row >> 5) * (kGammaBytes / 4) + (row & 7) * 4;
+        const int c8 = (row & 31) >> 3;
+        float a = 0.0f;
+#pragma unroll 8
+        for (int p = half * 64; p < half * 64 + 64; ++p)
+          a += *reinterpret_cast<const float *>(gcol + p * 128 + ((c8 ^ (p & 3)) << 5));
+        nk += a;
+      }
+      if (ct == 0 && valid && half == 0) {
+        const float l = ln2 * kLn2;
+        ln_out[n] = l;
+        lsum += (double)l;
+      }
+      if (i > 0)
+        ok = drain_stats<NKC>(i - 1, SFULL, SEMPTY, lane_q + kColStats, half, lane,
+                              k < K ? dst : nullptr);
+      ok = epi_sync_and(ok);  // gamma reads done before the next tile's writes
+    }
+    if (ok && T > 0)
+      ok = drain_stats<NKC>(T - 1, SFULL, SEMPTY, lane_q + kColStats, half, lane,
+                            k < K ? dst : nullptr);
+    ok = epi_sync_and(ok);
+    if (half == 1) nk_x[row] = nk;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+    if (lane == 0) lred[warp - 2] = lsum;
+    epi_sync_and(true);
+    if (k < K) {
+      if (!ok || T == 0) {
+        for (int f = half * DP; f < (half + 1) * DP; ++f) dst[f] = 0.0f;
+      }
+      if (half == 0) dst[2 * DP] = (ok && T > 0) ? nk + nk_x[row] : 0.0f;
+    }
+    if (warp == 2 && lane == 0) {
+      double t = 0.0;
+      for (int w = 0; w < kEpiWarps; ++w) t += lred[w];
+      ln_part[blockIdx.x] = t;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------------- host
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Row-major fp32 [rows][cols] matrix, box [box_rows][32] (128-byte rows) with the given swizzle.
+int make_map(CUtensorMap *m, const float *base, int64_t rows, int cols, int box_rows,
+             CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+  auto fn = encode_fn();
+  if (!fn) return fail(FGMM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * sizeof(float)};
+  cuuint32_t box[2] = {(cuuint32_t)KC, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FGMM_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return FGMM_OK;
+}
+
+struct TcPlan {
+  int64_t N;
+  int d, dp, KA, nkc, K, Kp, n_ct, n_pt, G, tpg, S, grid1, grid2;
+};
+
+TcPlan plan(int64_t N, int d, int K) {
+  TcPlan p{};
+  p.N = N; p.d = d; p.K = K;
+  p.dp = dp_of(d);
+  p.KA = 2 * p.dp;
+  p.nkc = p.KA / KC;
+  p.n_ct = (int)cdiv(K, NC);
+  p.Kp = p.n_ct * NC;
+  p.n_pt = (int)cdiv(N, BM);
+  const int sms = num_sms();
+  int G = (int)std::min<int64_t>(p.n_ct, std::max<int64_t>(1, cdiv(4 * sms, p.n_pt)));
+  p.tpg = (int)cdiv(p.n_ct, G);
+  p.G = (int)cdiv(p.n_ct, p.tpg);
+  p.grid1 = (int)std::min<int64_t>((int64_t)p.n_pt * p.G, sms);
+  p.S = std::max(1, std::min(sms / std::max(1, p.n_ct), p.n_pt));
+  p.grid2 = p.n_ct * p.S;
+  return p;
+}
+
+struct TcWs {
+  float *qhi, *qlo, *cst2, *part_m, *part_s, *partial;
+  double *ln_part;
+  size_t bytes;
+};
+
+TcWs tc_layout(void *ws, const TcPlan &p) {
+  TcWs w{};
+  Carve c(ws);
+  w.qhi = c.take<float>((size_t)p.Kp * p.KA);
+  w.qlo = c.take<float>((size_t)p.Kp * p.KA);
+  w.cst2 = c.take<float>(p.Kp);
+  w.part_m = c.take<float>((size_t)p.G * p.N);
+  w.part_s = c.take<float>((size_t)p.G * p.N);
+  w.partial = c.take<float>((size_t)p.S * p.K * (2 * p.dp + 4));
+  w.ln_part = c.take<double>(p.grid2);
+  w.bytes = c.bytes();
+  return w;
+}
+
+size_t smem1_bytes() { return 1024 + kStages1 * kStageBytes + 256 + 128 * 8; }
+size_t smem2_bytes() { return 1024 + kStages2 * kStageBytes + kGammaBytes + 1024; }
+
+template <int NKC>
+int tc_launch(const TcPlan &p, const float *pts, const TcWs &w, float *ln, cudaStream_t st) {
+  const float *phi = pts;
+  const float *plo = pts + points_half_floats(p.N, p.d);
+  const int64_t rows = npad_of(p.N);
+  CUtensorMap m_phi, m_plo, m_phi32, m_plo32, m_qhi, m_qlo;
+  int rc;
+  if ((rc = make_map(&m_phi, phi, rows, p.KA, BM))) return rc;
+  if ((rc = make_map(&m_plo, plo, rows, p.KA, BM))) return rc;
+  if ((rc = make_map(&m_phi32, phi, rows, p.KA, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))) return rc;
+  if ((rc = make_map(&m_plo32, plo, rows, p.KA, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))) return rc;
+  if ((rc = make_map(&m_qhi, w.qhi, p.Kp, p.KA, NC))) return rc;
+  if ((rc = make_map(&m_qlo, w.qlo, p.Kp, p.KA, NC))) return rc;
+  static bool attr_done[5] = {};
+  if (!attr_done[NKC / 2]) {
+    FGMM_CUDA_TRY(cudaFuncSetAttribute(tc_pass1_kernel<NKC>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1_bytes()));
+    FGMM_CUDA_TRY(cudaFuncSetAttribute(tc_pass2_kernel<NKC>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2_bytes()));
+    attr_done[NKC / 2] = true;
+  }
+  tc_pass1_kernel<NKC><<<p.grid1, kThreads, smem1_bytes(), st>>>(
+      m_phi, m_plo, m_qhi, m_qlo, w.cst2, p.N, p.n_pt, p.n_ct, p.G, p.tpg, w.part_m, w.part_s);
+  FGMM_LAUNCH_CHECK("tc_pass1_kernel");
+  mark(st, "tc_pass1_kernel");
+  tc_pass2_kernel<NKC><<<p.grid2, kThreads, smem2_bytes(), st>>>(
+      m_phi, m_plo, m_phi32, m_plo32, m_qhi, m_qlo, w.cst2, w.part_m, w.part_s, p.N, p.n_pt, p.G,
+      p.S, p.K, w.partial, ln, w.ln_part);
+  FGMM_LAUNCH_CHECK("tc_pass2_kernel");
+  mark(st, "tc_pass2_kernel");
+  return FGMM_OK;
+}
+
+}  // namespace
+
+int tc_launches(int64_t, int, int) { return 4; }
+
+bool tc_supported(int64_t N, int d, int K) { return N >= 1 && K >= 1 && d >= 1 && d <= kMaxDp; }
+
+size_t tc_points_bytes(int64_t N, int d) { return points_half_floats(N, d) * sizeof(float) * 2; }
+
+size_t tc_workspace_bytes(int64_t N, int d, int K) { return tc_layout(nullptr, plan(N, d, K)).bytes; }
+
+int tc_prepare_points(const float *X, int64_t N, int d, void *points, cudaStream_t st) {
+  const int dp = dp_of(d);
+  float *phi = static_cast<float *>(points);
+  float *plo = phi + points_half_floats(N, d);
+  const int64_t total = npad_of(N) * dp;
+  const int blocks = (int)std::min<int64_t>(cdiv(total, 256), 16 * num_sms());
+  tc_prep_points_kernel<<<blocks, 256, 0, st>>>(X, N, npad_of(N), d, dp, phi, plo);
+  FGMM_LAUNCH_CHECK("tc_prep_points_kernel");
+  return FGMM_OK;
+}
+
+int tc_em_stats(const float *X, const void *points, int64_t N, int d, const float *mu,
+                const float *var, const float *log_pi, int K, double *stats, float *log_norm,
+                void *ws, cudaStream_t st) {
+  (void)X;
+  const TcPlan p = plan(N, d, K);
+  const TcWs w = tc_layout(ws, p);
+  tc_prep_params_kernel<<<p.Kp, 128, 0, st>>>(mu, var, log_pi, K, d, p.dp, w.qhi, w.qlo, w.cst2);
+  FGMM_LAUNCH_CHECK("tc_prep_params_kernel");
+  mark(st, "tc_prep_params_kernel");
+  const float *pts = static_cast<const float *>(points);
+  int rc;
+  switch (p.nkc) {
+    case 2: rc = tc_launch<2>(p, pts, w, log_norm, st); break;
+    case 4: rc = tc_launch<4>(p, pts, w, log_norm, st); break;
+    case 6: rc = tc_launch<6>(p, pts, w, log_norm, st); break;
+    case 8: rc = tc_launch<8>(p, pts, w, log_norm, st); break;
+    default: return fail(FGMM_ERR_UNSUPPORTED, "tcgen05 family: d > 128");
+  }
+  if (rc) return rc;
+  return reduce_partials(w.partial, p.S, K, d, p.dp, 2 * p.dp + 4, w.ln_part, p.grid2, stats, st);
+}
+
+int tc_device_error(bool reset) {
+  int v = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  if (cudaMemcpyFromSymbol(&v, g_dev_error, sizeof(int)) != cudaSuccess) return -1;
+  if (reset && v) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_dev_error, &z, sizeof(int));
+  }
+  return v;
+}
+
 }  // namespace fgmm

@@ -8,49 +8,60 @@
 
 namespace fgmm {
 
-// partials: [slots][K][W] fp32 with W = 2d+1 laid out [s (d) | sq (d) | n];
-// stats: [n (K) | s (K d) | sq (K d) | sum ln].  One thread per (k, c).
+// partials: [slots][K][W] fp32, each row laid out [s (ds) | sq (ds) | n | ...] where only
+// the first d of each ds-wide run are meaningful; stats: [n (K) | s (K d) | sq (K d) | sum ln].
+// One thread per output value; the slots are summed in a fixed order with eight
+// independent loads in flight (deterministic).  Block 0 also sums the per-block
+// log-normalizer partials into the last entry.
 __global__ void reduce_partials_kernel(const float *__restrict__ part, int slots, int K, int d,
+                                       int ds, int W, const double *__restrict__ lnp, int ln_slots,
                                        double *__restrict__ stats) {
-  const int W = 2 * d + 1;
-  const int64_t total = (int64_t)K * W;
-  const int64_t slot_stride = total;
+  const int V = 2 * d + 1;
+  const int64_t total = (int64_t)K * V;
+  const int64_t slot_stride = (int64_t)K * W;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
-    double acc = 0.0;
-    for (int s = 0; s < slots; ++s) acc += (double)part[s * slot_stride + i];
-    const int k = (int)(i / W), c = (int)(i % W);
+    const int k = (int)(i / V), c = (int)(i % V);
+    int src;
     int64_t dst;
-    if (c < d)            dst = K + (int64_t)k * d + c;                       // s_k
-    else if (c < 2 * d)   dst = K + (int64_t)K * d + (int64_t)k * d + (c - d); // sq_k
-    else                  dst = k;                                            // n_k
+    if (c < d)          { src = c;               dst = K + (int64_t)k * d + c; }
+    else if (c < 2 * d) { src = ds + (c - d);    dst = K + (int64_t)K * d + (int64_t)k * d + (c - d); }
+    else                { src = 2 * ds;          dst = k; }
+    const float *p = part + (int64_t)k * W + src;
+    double acc = 0.0;
+    int s = 0;
+    for (; s + 8 <= slots; s += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = __ldg(p + (int64_t)(s + u) * slot_stride);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc += (double)v[u];
+    }
+    for (; s < slots; ++s) acc += (double)__ldg(p + (int64_t)s * slot_stride);
     stats[dst] = acc;
   }
-}
-
-__global__ void reduce_ln_kernel(const double *__restrict__ lnp, int n, double *__restrict__ out) {
-  __shared__ double sh[256];
-  double a = 0.0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) a += lnp[i];
-  sh[threadIdx.x] = a;
-  __syncthreads();
-  for (int s = blockDim.x / 2; s > 0; s >>= 1) {
-    if (threadIdx.x < s) sh[threadIdx.x] += sh[threadIdx.x + s];
+  if (blockIdx.x == 0) {
+    __shared__ double sh[256];
+    double a = 0.0;
+    for (int j = threadIdx.x; j < ln_slots; j += blockDim.x) a += lnp[j];
+    sh[threadIdx.x] = a;
     __syncthreads();
+    for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+      if (threadIdx.x < o) sh[threadIdx.x] += sh[threadIdx.x + o];
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) stats[total] = sh[0];
   }
-  if (threadIdx.x == 0) *out = sh[0];
 }
 
-int reduce_partials(const float *partials, int slots, int K, int d, const double *ln_partials,
-                    int ln_slots, double *stats, cudaStream_t stream) {
+int reduce_partials(const float *partials, int slots, int K, int d, int ds, int W,
+                    const double *ln_partials, int ln_slots, double *stats, cudaStream_t stream) {
   const int64_t total = (int64_t)K * (2 * d + 1);
-  int blocks = (int)std::min<int64_t>(cdiv(total, 256), 4 * num_sms());
-  reduce_partials_kernel<<<blocks, 256, 0, stream>>>(partials, slots, K, d, stats);
+  int blocks = (int)std::min<int64_t>(cdiv(total, 256), 8 * num_sms());
+  reduce_partials_kernel<<<blocks, 256, 0, stream>>>(partials, slots, K, d, ds, W, ln_partials,
+                                                     ln_slots, stats);
   FGMM_LAUNCH_CHECK("reduce_partials_kernel");
   mark(stream, "reduce_partials_kernel");
-  reduce_ln_kernel<<<1, 256, 0, stream>>>(ln_partials, ln_slots, stats + K + 2 * (int64_t)K * d);
-  FGMM_LAUNCH_CHECK("reduce_ln_kernel");
-  mark(stream, "reduce_ln_kernel");
   return FGMM_OK;
 }
 

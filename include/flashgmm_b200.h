@@ -94,6 +94,13 @@ int fgmm_em_fused(const float *X, int64_t N, int32_t d,
                   float *new_mu, float *new_var, float *new_log_pi, float *log_normalizer,
                   void *workspace, size_t workspace_bytes, void *stream);
 
+/* Synchronises the device and returns the code of the first failure a
+ * tensor-core kernel recorded (0 = none): every wait inside those kernels is
+ * bounded, and a wait that runs out records its code here and makes the kernel
+ * return instead of hanging.  reset != 0 clears the code.  Negative on a CUDA
+ * error.  Has no counterpart in the reference (its kernels have no waits). */
+int fgmm_device_error(int reset);
+
 /* Number of kernel launches one fgmm_em_stats call makes for this shape
  * (fgmm_em_update adds one more). */
 int fgmm_em_stats_launches(int64_t N, int32_t d, int32_t K);

@@ -24,3 +24,15 @@ def pytest_collection_modifyitems(config, items):
     for it in items:
         if "gpu" in it.keywords:
             it.add_marker(skip)
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error(request):
+    """Every GPU test must leave the kernels' bounded-wait error word at zero."""
+    yield
+    if "gpu" in request.keywords:
+        import torch
+        if torch.cuda.is_available():
+            from flashgmm_b200 import _lib
+            code = _lib.load().fgmm_device_error(1)
+            assert code == 0, f"a tensor-core kernel recorded wait-timeout code {code}"

@@ -7,8 +7,9 @@ CUDA error is within the stated absolute tolerance OR no worse than
 ``SLACK`` x the reference's own fp32 error (the reference is itself an fp32
 evaluation: at large |mu| / var its own error exceeds the 1e-4 / 1e-3 targets,
 see helpers.py).  Tolerances (one iteration):
-    mu 1e-4 (scale-aware relative), var 1e-4 (relative), log_pi 1e-4 (absolute),
-    log_normalizer 1e-3 (absolute); SLACK = 2.
+    mu 1e-4 (scale-aware relative), var 1e-4 (relative, well-conditioned
+    components), var_abs 1e-6 (|Δvar| / (mu^2 + var), all components),
+    log_pi 1e-4 (absolute), log_normalizer 1e-3 (absolute); SLACK = 2.
 """
 import numpy as np
 import pytest
@@ -19,18 +20,25 @@ from oracle import oracle
 
 pytestmark = pytest.mark.gpu
 
-TOL = {"mu": 1e-4, "var": 1e-4, "log_pi": 1e-4, "ln": 1e-3}
+TOL = {"mu": 1e-4, "var": 1e-4, "var_abs": 1e-6, "log_pi": 1e-4, "ln": 1e-3}
 SLACK = 2.0
 EM = [n for n in golden_names() if not n.startswith(("c1_fit20", "estep"))]
-FAMILIES = {"auto": 0, "simt": 1}
+FAMILIES = {"auto": 0, "simt": 1, "tc": 2}
 
 
 @pytest.fixture(params=list(FAMILIES))
 def family(request):
+    """Run each test with the default selection, the generic SIMT kernels and the
+    tcgen05 kernels (the latter only for shapes they cover: d <= 128)."""
     from flashgmm_b200 import flash_gmm_native as C
     prev = C.set_family(FAMILIES[request.param])
     yield request.param
     C.set_family(prev)
+
+
+def _skip_if_unsupported(family, d):
+    if family == "tc" and d > 128:
+        pytest.skip("tcgen05 family covers d <= 128")
 
 
 def run_gpu(g):
@@ -56,6 +64,7 @@ def check(name, got, g):
 @pytest.mark.parametrize("name", EM)
 def test_flash_em_fused_parity(name, family):
     g = load_golden(name)
+    _skip_if_unsupported(family, g["X"].shape[1])
     got = run_gpu(g)
     for a in got:
         assert np.all(np.isfinite(a))
@@ -117,7 +126,9 @@ def test_tail_and_padding_sizes(family):
     from flashgmm_b200.data import make_mixture, init_params
     dev = torch.device("cuda:0")
     for (N, K, d) in [(1, 1, 1), (129, 1, 32), (127, 129, 31), (300, 257, 64), (1000, 16, 96),
-                      (515, 33, 160), (64, 3, 200)]:
+                      (515, 33, 160), (64, 3, 200), (4000, 200, 128), (257, 384, 33)]:
+        if family == "tc" and d > 128:
+            continue
         X, *_ = make_mixture(N, K, d, seed=N * 7 + K)
         if K <= N:
             mu, var, lp = init_params(X, K, seed=3)
@@ -129,4 +140,5 @@ def test_tail_and_padding_sizes(family):
         got = [o.cpu().numpy() for o in C.flash_em_fused(X.to(dev), mu.to(dev), var.to(dev), lp.to(dev))]
         r64 = oracle.flash_em_fused_f64(X, mu, var, lp, with_stats=True)
         e = param_errors(got, r64[:4], n_k=r64[4], N=N)
-        assert e["ln"] < 1e-3 and e["log_pi"] < 1e-4 and e["mu"] < 1e-4 and e["var"] < 1e-3, (N, K, d, e)
+        ok = all(e[k] <= TOL[k] for k in TOL)
+        assert ok, (N, K, d, e)
