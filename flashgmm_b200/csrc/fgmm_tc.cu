@@ -54,7 +54,10 @@ constexpr int kStages2 = 2;
 constexpr int kTileBytes = BM * KC * 4;       // 16 KB: 128 rows x 128 B
 constexpr int kStageBytes = 4 * kTileBytes;   // 64 KB
 constexpr int kSubBytes = 32 * KC * 4;        // 4 KB: 32 rows x 128 B
-constexpr int kGammaBytes = NC * BM * 4;      // 64 KB
+constexpr int kGammaBytes = NC * BM * 4;      // 64 KB: gamma_hi and gamma_lo of 64 points
+constexpr int kRoundPts = 64;                 // points of a tile staged per gamma round
+constexpr int kGHalf = kGammaBytes / 2;       // 32 KB: one of gamma_hi / gamma_lo
+constexpr int kGAtom = kRoundPts * 128;       // 8 KB: 32 components x 64 points
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int kMaxDp = 128;                   // d <= 128 runs here
@@ -405,6 +408,11 @@ tc_pass2_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
   constexpr int PSTRIDE = 2 * DP + 4;
   constexpr int NB = (512 - KA) / NC;       // TMEM group buffers for the distance GEMM
   constexpr uint32_t kColStats = NB * NC;   // TMEM column of S[k, f]
+  // Per tile the MMA issues the first NP distance groups of the next tile, then the
+  // statistics of this tile, then the rest of the next tile (the producer loads in the
+  // same order): the statistics rounds never wait behind distance groups whose TMEM
+  // buffers only the next epilogue iteration frees.
+  constexpr int NP = NB < NKC ? NB : NKC;
   static_assert(NB >= 2, "TMEM budget");
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = align1024(smem_raw);
@@ -465,8 +473,8 @@ tc_pass2_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
         armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
         if (++stage == S) { stage = 0; phase ^= 1; }
       };
-      auto load_dist = [&](int pt) {
-        for (int c = 0; c < NKC && ok; ++c) {
+      auto load_dist = [&](int pt, int c0, int c1) {
+        for (int c = c0; c < c1 && ok; ++c) {
           const uint32_t base = acquire();
           if (!ok) return;
           mbar_arrive_expect_tx(FULL(stage), kStageBytes);
@@ -490,10 +498,11 @@ tc_pass2_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
           advance();
         }
       };
-      load_dist(p0);
+      load_dist(p0, 0, NKC);
       for (int i = 0; i < T && ok; ++i) {
-        if (i + 1 < T) load_dist(p0 + i + 1);
+        if (i + 1 < T) load_dist(p0 + i + 1, 0, NP);
         load_stats(p0 + i);
+        if (i + 1 < T) load_dist(p0 + i + 1, NP, NKC);
       }
       for (int s = 0; s < S; ++s)
         if (armed & (1u << s)) mbar_wait(FULL(s), (armed_par >> s) & 1u, kErrWaitDrain);
@@ -505,8 +514,8 @@ tc_pass2_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
       int stage = 0;
       uint32_t phase = 0, gcount = 0;
       bool ok = true;
-      auto issue_dist = [&]() {
-        for (int c = 0; c < NKC && ok; ++c) {
+      auto issue_dist = [&](int c0, int c1) {
+        for (int c = c0; c < c1 && ok; ++c) {
           if (!mbar_wait(FULL(stage), phase, kErrWaitFull)) { ok = false; return; }
           tc_fence_after();
           if (!issue_dist_chunk<NB>(smem_u32(smem + stage * kStageBytes), tmem, gcount, TFULL0,
@@ -515,35 +524,48 @@ tc_pass2_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
       };
+      // statistics of tile i in two gamma rounds of 64 points (two 32-point sub-chunks
+      // each); per 8 points: gamma_lo.F_hi and gamma_hi.F_lo, then gamma_hi.F_hi.
       auto issue_stats = [&](int i) {
-        if (!mbar_wait(GFULL, i & 1, kErrWaitGammaFull)) { ok = false; return; }
-        if (i > 0 && !mbar_wait(SEMPTY, (i - 1) & 1, kErrWaitStatsDone)) { ok = false; return; }
-        tc_fence_after();
-        for (int sub = 0; sub < BM / 32; ++sub) {
-          if (!mbar_wait(FULL(stage), phase, kErrWaitFull)) { ok = false; return; }
-          tc_fence_after();
-          const uint32_t base = smem_u32(smem + stage * kStageBytes);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            // gamma^T: MN-major (components contiguous), 4-point atoms of 512 B, component
-            // atoms 16 KB apart; F: MN-major (features contiguous), 4 KB per 32 features.
-            const uint64_t a = sdesc(gbase + (sub * 4 + kk) * 1024, kGammaBytes / 4, 512, kSw128Base32);
-            const uint64_t fh = sdesc(base + kk * 1024, kSubBytes, 512, kSw128Base32);
-            const uint64_t fl = sdesc(base + NKC * kSubBytes + kk * 1024, kSubBytes, 512, kSw128Base32);
-            mma_tf32(tmem + kColStats, a, fl, idesc_s, (sub | kk) ? 1u : 0u);
-            mma_tf32(tmem + kColStats, a, fh, idesc_s, 1u);
+        for (int r = 0; r < 2 && ok; ++r) {
+          const uint32_t rc = 2u * i + r;
+          if (!mbar_wait(GFULL, rc & 1u, kErrWaitGammaFull)) { ok = false; return; }
+          if (r == 0 && i > 0 && !mbar_wait(SEMPTY, (i - 1) & 1, kErrWaitStatsDone)) {
+            ok = false;
+            return;
           }
-          mma_commit(EMPTY(stage));
-          if (++stage == S) { stage = 0; phase ^= 1; }
+          tc_fence_after();
+          for (int s2 = 0; s2 < 2; ++s2) {
+            if (!mbar_wait(FULL(stage), phase, kErrWaitFull)) { ok = false; return; }
+            tc_fence_after();
+            const uint32_t base = smem_u32(smem + stage * kStageBytes);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              // gamma^T: MN-major (components contiguous), 4-point atoms of 512 B, component
+              // atoms 8 KB apart; F: MN-major (features contiguous), 4 KB per 32 features.
+              const uint32_t ga = gbase + (s2 * 4 + kk) * 1024;
+              const uint64_t ah = sdesc(ga, kGAtom, 512, kSw128Base32);
+              const uint64_t al = sdesc(ga + kGHalf, kGAtom, 512, kSw128Base32);
+              const uint64_t fh = sdesc(base + kk * 1024, kSubBytes, 512, kSw128Base32);
+              const uint64_t fl = sdesc(base + NKC * kSubBytes + kk * 1024, kSubBytes, 512, kSw128Base32);
+              mma_tf32(tmem + kColStats, al, fh, idesc_s, (r | s2 | kk) ? 1u : 0u);
+              mma_tf32(tmem + kColStats, ah, fl, idesc_s, 1u);
+              mma_tf32(tmem + kColStats, ah, fh, idesc_s, 1u);
+            }
+            mma_commit(EMPTY(stage));
+            if (++stage == S) { stage = 0; phase ^= 1; }
+          }
+          mma_commit(GEMPTY);
         }
-        mma_commit(GEMPTY);
         mma_commit(SFULL);
       };
-      issue_dist();
+      issue_dist(0, NKC);
       for (int i = 0; i < T && ok; ++i) {
-        if (i + 1 < T) issue_dist();
+        if (i + 1 < T) issue_dist(0, NP);
         if (!ok) break;
         issue_stats(i);
+        if (!ok) break;
+        if (i + 1 < T) issue_dist(NP, NKC);
       }
       if (!ok) {
         mma_commit(SFULL);  // flush whatever was issued before giving up
@@ -580,74 +602,101 @@ tc_pass2_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
 #pragma unroll 1
       for (int grp = 1; grp < NKC - 1 && ok; ++grp)
         ok = drain_group<NB, false>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
-      ok = ok && __all_sync(0xffffffffu, mbar_wait(GEMPTY, (i & 1) ^ 1, kErrWaitGammaEmpty));
-      // The last K group is drained straight into gamma, 16 columns at a time: summed,
-      // turned into gamma = 2^(l2 - ln2) (tf32) and stored as the MN-major
-      // SWIZZLE_128B_BASE32B operand gamma^T (M = component, K = point): point p owns the
-      // 128-byte row p of each 32-component atom; its four 32-byte chunks (8 components
-      // each) sit at chunk index (c8 ^ (p % 4)); component atoms are 16 KB apart.  The two
-      // 16-byte halves of a chunk are stored in an order that differs between rows p and
-      // p+4, so a warp's stores hit every bank once per 128 bytes.
+      // The last K group is drained straight into gamma = 2^(l2 - ln2) (fp32, in acc).
       if (ok) {
         const uint32_t buf = gcount % NB, use = gcount / NB;
         ok = __all_sync(0xffffffffu, mbar_wait(TFULL0 + 8u * buf, use & 1u, kErrWaitTmemFull));
         if (ok) {
           tc_fence_after();
-          uint8_t *grow = gamma + row * 128;
-          const int flip = (row >> 2) & 1;
 #pragma unroll
           for (int hh = 0; hh < kHalf / 16; ++hh) {
-            const int jj = hh >> 1;
             float v[16];
             tmem_ld16(lane_tmem + buf * NC + hh * 16, v);
             tmem_wait_ld();
 #pragma unroll
-            for (int c2 = 0; c2 < 2; ++c2) {
-              const int c8 = (hh & 1) * 2 + c2;
-              float gq[8];
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const int col = hh * 16 + c2 * 8 + e;
-                const float l2 = fmaf(acc[col] + v[c2 * 8 + e], -0.5f * kLog2e, cp[col]);
-                gq[e] = valid ? to_tf32(ex2(l2 - ln2)) : 0.0f;
-              }
-              uint8_t *chunk = grow + (half * 2 + jj) * (kGammaBytes / 4) + ((c8 ^ (row & 3)) << 5);
-              const float4 lo4 = make_float4(gq[0], gq[1], gq[2], gq[3]);
-              const float4 hi4 = make_float4(gq[4], gq[5], gq[6], gq[7]);
-              *reinterpret_cast<float4 *>(chunk + (flip << 4)) = flip ? hi4 : lo4;
-              *reinterpret_cast<float4 *>(chunk + ((flip ^ 1) << 4)) = flip ? lo4 : hi4;
+            for (int e = 0; e < 16; ++e) {
+              const int col = hh * 16 + e;
+              const float l2 = fmaf(acc[col] + v[e], -0.5f * kLog2e, cp[col]);
+              acc[col] = valid ? ex2(l2 - ln2) : 0.0f;
             }
           }
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(TEMPTY0 + 8u * buf);
           ++gcount;
-          fence_proxy_async_smem();
         }
       }
-      ok = epi_sync_and(ok);  // every row of gamma is in place
+      // the previous tile's statistics leave TMEM before this tile's rounds start
+      if (ok && i > 0)
+        ok = drain_stats<NKC>(i - 1, SFULL, SEMPTY, lane_q + kColStats, half, lane,
+                              k < K ? dst : nullptr);
+      ok = epi_sync_and(ok);
       if (!ok) break;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(GFULL);
-      {  // n_k: column `row` of gamma^T summed over this warp half's 64 points (the same
-         // tf32-rounded weights the statistics GEMM consumes)
-        const uint8_t *gcol = gamma + (row >> 5) * (kGammaBytes / 4) + (row & 7) * 4;
-        const int c8 = (row & 31) >> 3;
-        float a = 0.0f;
+      // Two rounds of 64 points: the round's rows store gamma_hi = tf32(gamma) and
+      // gamma_lo = tf32(gamma - gamma_hi) as MN-major SWIZZLE_128B_BASE32B operands
+      // gamma^T (M = component, K = point): point p' owns the 128-byte row p' of each
+      // 32-component atom (atoms 8 KB apart); its four 32-byte chunks (8 components each)
+      // sit at chunk index (c8 ^ (p' % 4)).  The two 16-byte halves of a chunk are stored
+      // in an order that differs between rows p' and p'+4, so a warp's stores hit every
+      // bank once per 128 bytes.  n_k adds gamma_hi + gamma_lo of the round's points.
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const uint32_t rc = 2u * i + r;
+        ok = __all_sync(0xffffffffu, mbar_wait(GEMPTY, (rc & 1u) ^ 1u, kErrWaitGammaEmpty));
+        if (ok && (row >> 6) == r) {
+          const int rp = row & (kRoundPts - 1);
+          uint8_t *grow = gamma + rp * 128;
+          const int flip = (rp >> 2) & 1;
+#pragma unroll
+          for (int jj = 0; jj < kHalf / 32; ++jj) {
+#pragma unroll
+            for (int c8 = 0; c8 < 4; ++c8) {
+              float gh[8], gl[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float g = acc[jj * 32 + c8 * 8 + e];
+                gh[e] = to_tf32(g);
+                gl[e] = to_tf32(g - gh[e]);
+              }
+              uint8_t *chunk = grow + (half * 2 + jj) * kGAtom + ((c8 ^ (rp & 3)) << 5);
+              const int o0 = flip << 4, o1 = (flip ^ 1) << 4;
+              *reinterpret_cast<float4 *>(chunk + o0) =
+                  flip ? make_float4(gh[4], gh[5], gh[6], gh[7]) : make_float4(gh[0], gh[1], gh[2], gh[3]);
+              *reinterpret_cast<float4 *>(chunk + o1) =
+                  flip ? make_float4(gh[0], gh[1], gh[2], gh[3]) : make_float4(gh[4], gh[5], gh[6], gh[7]);
+              *reinterpret_cast<float4 *>(chunk + kGHalf + o0) =
+                  flip ? make_float4(gl[4], gl[5], gl[6], gl[7]) : make_float4(gl[0], gl[1], gl[2], gl[3]);
+              *reinterpret_cast<float4 *>(chunk + kGHalf + o1) =
+                  flip ? make_float4(gl[0], gl[1], gl[2], gl[3]) : make_float4(gl[4], gl[5], gl[6], gl[7]);
+            }
+          }
+          fence_proxy_async_smem();
+        }
+        ok = epi_sync_and(ok);  // every row of the round is in place
+        if (!ok) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(GFULL);
+        {
+          const uint8_t *gcol = gamma + (row >> 5) * kGAtom + (row & 7) * 4;
+          const int c8 = (row & 31) >> 3;
+          float a = 0.0f;
 #pragma unroll 8
-        for (int p = half * 64; p < half * 64 + 64; ++p)
-          a += *reinterpret_cast<const float *>(gcol + p * 128 + ((c8 ^ (p & 3)) << 5));
-        nk += a;
+          for (int pp = half * 32; pp < half * 32 + 32; ++pp) {
+            const int off = pp * 128 + ((c8 ^ (pp & 3)) << 5);
+            a += *reinterpret_cast<const float *>(gcol + off) +
+                 *reinterpret_cast<const float *>(gcol + kGHalf + off);
+          }
+          nk += a;
+        }
+        ok = epi_sync_and(ok);  // gamma reads done before the next round's writes
+        if (!ok) break;
       }
+      if (!ok) break;
       if (ct == 0 && valid && half == 0) {
         const float l = ln2 * kLn2;
         ln_out[n] = l;
         lsum += (double)l;
       }
-      if (i > 0)
-        ok = drain_stats<NKC>(i - 1, SFULL, SEMPTY, lane_q + kColStats, half, lane,
-                              k < K ? dst : nullptr);
-      ok = epi_sync_and(ok);  // gamma reads done before the next tile's writes
     }
     if (ok && T > 0)
       ok = drain_stats<NKC>(T - 1, SFULL, SEMPTY, lane_q + kColStats, half, lane,
