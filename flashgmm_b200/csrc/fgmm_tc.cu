@@ -16,12 +16,12 @@
 //   per point and component group.
 // Pass 2 (statistics): CTA (component tile ct, slot) walks a contiguous range of point
 //   tiles.  Per tile: the distance GEMM again -> gamma = 2^(l2 - ln2) computed by the
-//   epilogue from TMEM and stored to shared memory (rounded to tf32) -> a second GEMM
-//   S[k, f] = sum_n gamma[n,k] F[n,f],  F[n] = [x^2 | x] (hi + lo: 2 products), and
-//   n_k = sum_n gamma[n,k] on the CUDA cores from the same rounded weights.  S is
-//   restarted every tile and added (fp32, round-to-nearest) into one partial row per
-//   CTA; the partials are reduced in fp64 afterwards: deterministic, no atomics
-//   between CTAs.  (Reference: flash_accumulate_stats_v2_kernel,
+//   epilogue from TMEM and stored to shared memory -> a second GEMM
+//   S[k, f] = sum_n gamma[n,k] F[n,f],  F[n] = [x^2 | x] (hi + lo), and
+//   n_k = sum_n gamma[n,k] on the CUDA cores.  gamma is split into tf32 hi + lo (three
+//   products) and staged in two 64-point rounds; S restarts every tile and is added
+//   (fp32, round-to-nearest) into one partial row per CTA; the partials are reduced in
+//   fp64 afterwards: deterministic, no atomics between CTAs.  (Reference: flash_accumulate_stats_v2_kernel,
 //   flash_gmm/csrc/flash_gmm_cuda.cu:179-292, which accumulates with global atomics.)
 //
 // Warp roles (320 threads): warp 0 issues TMA loads, warp 1 owns TMEM and issues
@@ -97,14 +97,18 @@ __global__ void tc_prep_points_kernel(const float *__restrict__ X, int64_t N, in
 
 // Q[k] = [iv (dp) | -2 mu iv (dp)] (hi/lo of the fp64 value), cst2[k]; rows k >= K are
 // zero with cst2 = -inf (padding components never receive responsibility).
+// Also writes the direct-form parameters the refinement uses: sc = var^{-1/2},
+// ms = mu sc, lc = log_pi - 1/2 (d log 2pi + sum log var)  ([K][d], [K][d], [K]).
 __global__ void tc_prep_params_kernel(const float *__restrict__ mu, const float *__restrict__ var,
                                       const float *__restrict__ log_pi, int K, int d, int dp,
                                       float *__restrict__ qhi, float *__restrict__ qlo,
-                                      float *__restrict__ cst2) {
+                                      float *__restrict__ cst2, float *__restrict__ sc,
+                                      float *__restrict__ ms, float *__restrict__ lc) {
   const int k = blockIdx.x;
   const int KA = 2 * dp;
-  __shared__ double red[8];
-  double acc = 0.0;  // sum_j (log var + mu^2 / var)
+  __shared__ double red[8], red2[8];
+  double acc = 0.0;   // sum_j (log var + mu^2 / var)
+  double acc2 = 0.0;  // sum_j log var
   for (int j = threadIdx.x; j < dp; j += blockDim.x) {
     double iv = 0.0, b = 0.0;
     if (k < K && j < d) {
@@ -113,6 +117,10 @@ __global__ void tc_prep_params_kernel(const float *__restrict__ mu, const float 
       iv = 1.0 / v;
       b = -2.0 * m * iv;
       acc += log(v) + m * m * iv;
+      acc2 += log(v);
+      const double sv = 1.0 / sqrt(v);
+      sc[(int64_t)k * d + j] = (float)sv;
+      ms[(int64_t)k * d + j] = (float)(m * sv);
     }
     const float ivh = to_tf32((float)iv), bh = to_tf32((float)b);
     qhi[(int64_t)k * KA + j] = ivh;
@@ -121,15 +129,19 @@ __global__ void tc_prep_params_kernel(const float *__restrict__ mu, const float 
     qlo[(int64_t)k * KA + dp + j] = to_tf32((float)(b - (double)bh));
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  for (int o = 16; o > 0; o >>= 1) {
+    acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    acc2 += __shfl_xor_sync(0xffffffffu, acc2, o);
+  }
+  if ((threadIdx.x & 31) == 0) { red[threadIdx.x >> 5] = acc; red2[threadIdx.x >> 5] = acc2; }
   __syncthreads();
   if (threadIdx.x == 0) {
-    double t = 0.0;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+    double t = 0.0, t2 = 0.0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { t += red[w]; t2 += red2[w]; }
     cst2[k] = (k < K) ? (float)(1.4426950408889634 *
                                 ((double)log_pi[k] - 0.5 * (d * kLog2Pi + t)))
                       : -INFINITY;
+    if (k < K) lc[k] = (float)((double)log_pi[k] - 0.5 * (d * kLog2Pi + t2));
   }
 }
 
@@ -214,7 +226,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ CUtensorMap tm_plo,
                 const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant__ CUtensorMap tm_qlo,
                 const float *__restrict__ cst2, int64_t N, int n_pt, int n_ct, int G, int tpg,
-                float *__restrict__ part_m, float *__restrict__ part_s) {
+                float *__restrict__ part_m, float *__restrict__ part_s,
+                float2 *__restrict__ part_tv, int2 *__restrict__ part_ti) {
   constexpr int S = kStages1;
   constexpr int NB = 4;  // TMEM group buffers (4 x 128 columns)
   extern __shared__ uint8_t smem_raw[];
@@ -222,7 +235,8 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * kStageBytes);
   // bars: full[S] empty[S] tfull[NB] tempty[NB] done
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 2 * NB + 1);
-  float2 *lse_x = reinterpret_cast<float2 *>(tmem_slot + 2);  // [128] half-row LSE exchange
+  struct Half { float m, s, v1, v2; int i1, i2; };
+  Half *lse_x = reinterpret_cast<Half *>(tmem_slot + 2);  // [128] half-row exchange
   const uint32_t bar0 = smem_u32(bars);
   auto FULL = [&](int s) { return bar0 + 8u * s; };
   auto EMPTY = [&](int s) { return bar0 + 8u * (S + s); };
@@ -310,6 +324,8 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
       const int pt = u / G, g = u % G;
       const int t1 = min(n_ct, (g + 1) * tpg);
       float m = -INFINITY, s = 0.0f;
+      float v1 = -INFINITY, v2 = -INFINITY;  // the row's two largest log2-likelihoods
+      int i1 = -1, i2 = -1;
       for (int t = g * tpg; t < t1 && ok; ++t) {
         float acc[kHalf];
         ok = drain_group<NB, true>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
@@ -333,20 +349,44 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
           for (int e = 0; e < 32; ++e) a += ex2(acc[j * 32 + e] - mr);
           s = a;
           m = mn;
+          if (cm > v2) {  // rare once the row's leading components are known
+            const int kb = t * NC + half * kHalf + j * 32;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const float x = acc[j * 32 + e];
+              if (x > v2) {
+                if (x > v1) { v2 = v1; i2 = i1; v1 = x; i1 = kb + e; }
+                else        { v2 = x; i2 = kb + e; }
+              }
+            }
+          }
         }
       }
       // merge the two column halves of each row
-      if (half == 1) lse_x[row] = make_float2(m, s);
+      if (half == 1) lse_x[row] = Half{m, s, v1, v2, i1, i2};
       ok = epi_sync_and(ok);
       if (half == 0) {
-        const float2 o = lse_x[row];
-        const float mn = fmaxf(m, o.x);
+        const Half o = lse_x[row];
+        const float mn = fmaxf(m, o.m);
         const float mr = (mn == -INFINITY) ? 0.0f : mn;
-        const float sm = s * ex2(m - mr) + o.y * ex2(o.x - mr);
+        const float sm = s * ex2(m - mr) + o.s * ex2(o.m - mr);
+        float c[4] = {v1, v2, o.v1, o.v2};
+        int ci[4] = {i1, i2, o.i1, o.i2};
+        float b1 = -INFINITY, b2 = -INFINITY;
+        int j1 = -1, j2 = -1;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (c[e] > b2) {
+            if (c[e] > b1) { b2 = b1; j2 = j1; b1 = c[e]; j1 = ci[e]; }
+            else           { b2 = c[e]; j2 = ci[e]; }
+          }
+        }
         const int64_t n = (int64_t)pt * BM + row;
         if (ok && n < N) {
           part_m[(int64_t)g * N + n] = mn;
           part_s[(int64_t)g * N + n] = sm;
+          part_tv[(int64_t)g * N + n] = make_float2(b1, b2);
+          part_ti[(int64_t)g * N + n] = make_int2(j1, j2);
         }
       }
       ok = epi_sync_and(ok);
@@ -360,13 +400,117 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
   }
 }
 
+// ------------------------------------------------------------------------- refine
+// Exact re-evaluation of each point's two leading components.  The tensor-core
+// log-likelihoods carry an absolute error of ~1e-4..1e-3 (the expanded form's terms
+// |x|^2/var are far larger than the Mahalanobis distance they cancel down to), while
+// responsibility mass sits on one or two components per point.  This kernel merges the
+// pass-1 partials of the component groups, recomputes the two leading log-likelihoods in
+// the direct form of flash_gmm/csrc/flash_gmm_cpu.cpp:30-45 (fp32, with
+// w = x var^{-1/2} - mu var^{-1/2} formed by one FMA), swaps them into the log-sum-exp,
+// and writes the log-normalizer (output and log2 form for pass 2), the two exact
+// log2-likelihoods with their component indices, and one log-normalizer sum per block.
+// Eight lanes per point (four points per warp), lanes striped over the dimensions; all
+// loads of a point are issued before its reductions.
+template <int DPL>  // dimensions per lane: ceil(d / 8)
+__global__ void __launch_bounds__(256)
+tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__restrict__ sc,
+                 const float *__restrict__ ms, const float *__restrict__ lc,
+                 const float *__restrict__ part_m, const float *__restrict__ part_s,
+                 const float2 *__restrict__ part_tv, const int2 *__restrict__ part_ti, int G,
+                 float *__restrict__ ln2x, int2 *__restrict__ top_i, float2 *__restrict__ top_l,
+                 float *__restrict__ ln_out, double *__restrict__ ln_part) {
+  __shared__ double wsum[8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int sub = lane & 7;           // lane within the point's group of 8
+  double acc = 0.0;
+  const int64_t stride = (int64_t)gridDim.x * 32;  // points per grid sweep
+  for (int64_t n = ((int64_t)blockIdx.x * 8 + warp) * 4 + (lane >> 3); n - (lane >> 3) < N;
+       n += stride) {
+    const bool live = n < N;
+    const int64_t nn = live ? n : 0;
+    float mx = -INFINITY, b1 = -INFINITY, b2 = -INFINITY;
+    int j1 = -1, j2 = -1;
+    for (int g = 0; g < G; ++g) {
+      mx = fmaxf(mx, __ldg(part_m + (int64_t)g * N + nn));
+      const float2 tv = part_tv[(int64_t)g * N + nn];
+      const int2 ti = part_ti[(int64_t)g * N + nn];
+      if (ti.x >= 0 && tv.x > b2) {
+        if (tv.x > b1) { b2 = b1; j2 = j1; b1 = tv.x; j1 = ti.x; }
+        else           { b2 = tv.x; j2 = ti.x; }
+      }
+      if (ti.y >= 0 && tv.y > b2) {
+        if (tv.y > b1) { b2 = b1; j2 = j1; b1 = tv.y; j1 = ti.y; }
+        else           { b2 = tv.y; j2 = ti.y; }
+      }
+    }
+    float sm = 0.0f;
+    for (int g = 0; g < G; ++g)
+      sm += __ldg(part_s + (int64_t)g * N + nn) * ex2(__ldg(part_m + (int64_t)g * N + nn) - mx);
+    const int k1 = j1 >= 0 ? j1 : 0, k2 = j2 >= 0 ? j2 : 0;
+    float x[DPL], s1[DPL], m1[DPL], s2[DPL], m2[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+      const int j = sub + 8 * i;
+      const bool in = j < d;
+      x[i] = in ? __ldg(X + nn * d + j) : 0.0f;
+      s1[i] = in ? __ldg(sc + (int64_t)k1 * d + j) : 0.0f;
+      m1[i] = in ? __ldg(ms + (int64_t)k1 * d + j) : 0.0f;
+      s2[i] = in ? __ldg(sc + (int64_t)k2 * d + j) : 0.0f;
+      m2[i] = in ? __ldg(ms + (int64_t)k2 * d + j) : 0.0f;
+    }
+    float p1 = 0.0f, p2 = 0.0f;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+      const float w1 = fmaf(x[i], s1[i], -m1[i]);
+      const float w2 = fmaf(x[i], s2[i], -m2[i]);
+      p1 = fmaf(w1, w1, p1);
+      p2 = fmaf(w2, w2, p2);
+    }
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) {
+      p1 += __shfl_xor_sync(0xffffffffu, p1, o);
+      p2 += __shfl_xor_sync(0xffffffffu, p2, o);
+    }
+    const float e1 = j1 >= 0 ? (__ldg(lc + k1) - 0.5f * p1) * kLog2e : -INFINITY;
+    const float e2 = j2 >= 0 ? (__ldg(lc + k2) - 0.5f * p2) * kLog2e : -INFINITY;
+    // swap the approximate leading terms of the sum for the exact ones
+    const float m = fmaxf(mx, fmaxf(e1, e2));
+    float rest = sm * ex2(mx - m);
+    if (j1 >= 0) rest -= ex2(b1 - m);
+    if (j2 >= 0) rest -= ex2(b2 - m);
+    float tot = fmaxf(rest, 0.0f);
+    if (j1 >= 0) tot += ex2(e1 - m);
+    if (j2 >= 0) tot += ex2(e2 - m);
+    const float ln2 = m + __log2f(tot);
+    if (live && sub == 0) {
+      ln2x[n] = ln2;
+      top_i[n] = make_int2(j1, j2);
+      top_l[n] = make_float2(e1, e2);
+      const float l = ln2 * kLn2;
+      ln_out[n] = l;
+      acc += (double)l;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) wsum[warp] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < 8; ++w) t += wsum[w];
+    ln_part[blockIdx.x] = t;
+  }
+}
+
 // ------------------------------------------------------------------------- pass 2
-// Add (or, for the first tile j == 0, store) the TMEM statistics of tile j into the CTA's
+// Add (or, for the CTA's first tile j == 0, store) the TMEM statistics of tile j into the CTA's
 // partial row `dst` ([s (DP) | sq (DP) | n | pad]); warp half 0 takes the x^2 features
 // (-> sq), half 1 the x features (-> s).  dst == nullptr: padding component, no store.
-template <int NKC>
+template <int NKC, bool kTwo>
 __device__ __forceinline__ bool drain_stats(int j, uint32_t sfull, uint32_t sempty,
-                                            uint32_t stats_tmem, int half, int lane, float *dst) {
+                                            uint32_t stats_tmem, uint32_t stats_tmem1, int half,
+                                            int lane, float *dst) {
   constexpr int DP = NKC * KC / 2;
   if (!__all_sync(0xffffffffu, mbar_wait(sfull, j & 1, kErrWaitStatsDone))) return false;
   tc_fence_after();
@@ -375,6 +519,13 @@ __device__ __forceinline__ bool drain_stats(int j, uint32_t sfull, uint32_t semp
     float v[32];
     tmem_ld32(stats_tmem + c * 32, v);
     tmem_wait_ld();
+    if (kTwo) {
+      float w[32];
+      tmem_ld32(stats_tmem1 + c * 32, w);
+      tmem_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 32; ++e) v[e] += w[e];
+    }
     if (dst) {
       float *o = dst + (half == 0 ? DP + c * 32 : c * 32 - DP);
 #pragma unroll
@@ -398,20 +549,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 tc_pass2_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ CUtensorMap tm_plo,
                 const __grid_constant__ CUtensorMap tm_phi32, const __grid_constant__ CUtensorMap tm_plo32,
                 const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant__ CUtensorMap tm_qlo,
-                const float *__restrict__ cst2, const float *__restrict__ part_m,
-                const float *__restrict__ part_s, int64_t N, int n_pt, int G, int S_slots, int K,
-                float *__restrict__ partial, float *__restrict__ ln_out,
-                double *__restrict__ ln_part) {
+                const float *__restrict__ cst2, const float *__restrict__ ln2x,
+                const int2 *__restrict__ top_i, const float2 *__restrict__ top_l, int64_t N,
+                int n_pt, int S_slots, int K, float *__restrict__ partial) {
   constexpr int S = kStages2;
   constexpr int KA = NKC * KC;
   constexpr int DP = KA / 2;
   constexpr int PSTRIDE = 2 * DP + 4;
-  constexpr int NB = (512 - KA) / NC;       // TMEM group buffers for the distance GEMM
-  constexpr uint32_t kColStats = NB * NC;   // TMEM column of S[k, f]
-  // Per tile the MMA issues the first NP distance groups of the next tile, then the
-  // statistics of this tile, then the rest of the next tile (the producer loads in the
-  // same order): the statistics rounds never wait behind distance groups whose TMEM
-  // buffers only the next epilogue iteration frees.
+  // For KA <= 128 TMEM holds two statistics regions: rounds 0 and 1 accumulate
+  // separately (half the additions each, at half the magnitude) and the drain adds them
+  // in fp32.
+  constexpr int NSR = KA <= 128 ? 2 : 1;
+  constexpr int NB = (512 - NSR * KA) / NC;  // TMEM group buffers for the distance GEMM
+  constexpr uint32_t kColStats = NB * NC;    // TMEM column of S[k, f] (round 0 region)
+  constexpr uint32_t kColStats1 = kColStats + (NSR == 2 ? KA : 0);  // round 1 region
+  // Per tile the MMA issues the first NP distance groups of the next tile, statistics
+  // round 0 of this tile, the rest of the next tile, statistics round 1 (the producer
+  // loads in the same order): no round waits behind distance groups whose TMEM buffers
+  // only the next epilogue iteration frees, and the tensor pipe has distance work while
+  // the epilogue prepares round 1.
   constexpr int NP = NB < NKC ? NB : NKC;
   static_assert(NB >= 2, "TMEM budget");
   extern __shared__ uint8_t smem_raw[];
@@ -485,8 +641,8 @@ tc_pass2_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
           advance();
         }
       };
-      auto load_stats = [&](int pt) {
-        for (int sub = 0; sub < BM / 32 && ok; ++sub) {
+      auto load_stats = [&](int pt, int r) {
+        for (int sub = 2 * r; sub < 2 * r + 2 && ok; ++sub) {
           const uint32_t base = acquire();
           if (!ok) return;
           mbar_arrive_expect_tx(FULL(stage), 2 * NKC * kSubBytes);
@@ -501,8 +657,9 @@ tc_pass2_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
       load_dist(p0, 0, NKC);
       for (int i = 0; i < T && ok; ++i) {
         if (i + 1 < T) load_dist(p0 + i + 1, 0, NP);
-        load_stats(p0 + i);
+        load_stats(p0 + i, 0);
         if (i + 1 < T) load_dist(p0 + i + 1, NP, NKC);
+        load_stats(p0 + i, 1);
       }
       for (int s = 0; s < S; ++s)
         if (armed & (1u << s)) mbar_wait(FULL(s), (armed_par >> s) & 1u, kErrWaitDrain);
@@ -524,48 +681,61 @@ tc_pass2_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
       };
-      // statistics of tile i in two gamma rounds of 64 points (two 32-point sub-chunks
-      // each); per 8 points: gamma_lo.F_hi and gamma_hi.F_lo, then gamma_hi.F_hi.
-      auto issue_stats = [&](int i) {
-        for (int r = 0; r < 2 && ok; ++r) {
-          const uint32_t rc = 2u * i + r;
-          if (!mbar_wait(GFULL, rc & 1u, kErrWaitGammaFull)) { ok = false; return; }
-          if (r == 0 && i > 0 && !mbar_wait(SEMPTY, (i - 1) & 1, kErrWaitStatsDone)) {
-            ok = false;
-            return;
-          }
-          tc_fence_after();
-          for (int s2 = 0; s2 < 2; ++s2) {
-            if (!mbar_wait(FULL(stage), phase, kErrWaitFull)) { ok = false; return; }
-            tc_fence_after();
-            const uint32_t base = smem_u32(smem + stage * kStageBytes);
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              // gamma^T: MN-major (components contiguous), 4-point atoms of 512 B, component
-              // atoms 8 KB apart; F: MN-major (features contiguous), 4 KB per 32 features.
-              const uint32_t ga = gbase + (s2 * 4 + kk) * 1024;
-              const uint64_t ah = sdesc(ga, kGAtom, 512, kSw128Base32);
-              const uint64_t al = sdesc(ga + kGHalf, kGAtom, 512, kSw128Base32);
-              const uint64_t fh = sdesc(base + kk * 1024, kSubBytes, 512, kSw128Base32);
-              const uint64_t fl = sdesc(base + NKC * kSubBytes + kk * 1024, kSubBytes, 512, kSw128Base32);
-              mma_tf32(tmem + kColStats, al, fh, idesc_s, (r | s2 | kk) ? 1u : 0u);
-              mma_tf32(tmem + kColStats, ah, fl, idesc_s, 1u);
-              mma_tf32(tmem + kColStats, ah, fh, idesc_s, 1u);
-            }
-            mma_commit(EMPTY(stage));
-            if (++stage == S) { stage = 0; phase ^= 1; }
-          }
-          mma_commit(GEMPTY);
+      // Statistics round r of tile i: 64 points in two staged 32-point sub-chunks.  The
+      // TMEM statistics restart every tile (the epilogue flushes them after round 1), and
+      // within a round all small products (gamma_lo.F_hi, gamma_hi.F_lo) go before the
+      // gamma_hi.F_hi ones, which keeps additions at the accumulator's full magnitude few.
+      auto issue_round = [&](int i, int r) {
+        const uint32_t rc = 2u * i + r;
+        if (!mbar_wait(GFULL, rc & 1u, kErrWaitGammaFull)) { ok = false; return; }
+        if (r == 0 && i > 0 && !mbar_wait(SEMPTY, (i - 1) & 1u, kErrWaitStatsDone)) {
+          ok = false;
+          return;
         }
-        mma_commit(SFULL);
+        uint32_t base[2];
+        int st[2];
+        for (int s2 = 0; s2 < 2; ++s2) {
+          if (!mbar_wait(FULL(stage), phase, kErrWaitFull)) { ok = false; return; }
+          base[s2] = smem_u32(smem + stage * kStageBytes);
+          st[s2] = stage;
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+        tc_fence_after();
+        const uint32_t dstat = tmem + (r == 0 ? kColStats : kColStats1);
+        const uint32_t first = NSR == 2 ? 0u : (uint32_t)r;  // round restarts its region
+        // gamma^T: MN-major (components contiguous), 4-point atoms of 512 B, component
+        // atoms 8 KB apart; F: MN-major (features contiguous), 4 KB per 32 features.
+#pragma unroll
+        for (int s2 = 0; s2 < 2; ++s2)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t ga = gbase + (s2 * 4 + kk) * 1024;
+            const uint64_t ah = sdesc(ga, kGAtom, 512, kSw128Base32);
+            const uint64_t al = sdesc(ga + kGHalf, kGAtom, 512, kSw128Base32);
+            const uint64_t fh = sdesc(base[s2] + kk * 1024, kSubBytes, 512, kSw128Base32);
+            const uint64_t fl = sdesc(base[s2] + NKC * kSubBytes + kk * 1024, kSubBytes, 512, kSw128Base32);
+            mma_tf32(dstat, al, fh, idesc_s, (first | s2 | kk) ? 1u : 0u);
+            mma_tf32(dstat, ah, fl, idesc_s, 1u);
+          }
+#pragma unroll
+        for (int s2 = 0; s2 < 2; ++s2)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t ah = sdesc(gbase + (s2 * 4 + kk) * 1024, kGAtom, 512, kSw128Base32);
+            const uint64_t fh = sdesc(base[s2] + kk * 1024, kSubBytes, 512, kSw128Base32);
+            mma_tf32(dstat, ah, fh, idesc_s, 1u);
+          }
+        mma_commit(EMPTY(st[0]));
+        mma_commit(EMPTY(st[1]));
+        mma_commit(GEMPTY);
+        if (r == 1) mma_commit(SFULL);
       };
       issue_dist(0, NKC);
       for (int i = 0; i < T && ok; ++i) {
         if (i + 1 < T) issue_dist(0, NP);
-        if (!ok) break;
-        issue_stats(i);
-        if (!ok) break;
-        if (i + 1 < T) issue_dist(NP, NKC);
+        if (ok) issue_round(i, 0);
+        if (ok && i + 1 < T) issue_dist(NP, NKC);
+        if (ok) issue_round(i, 1);
       }
       if (!ok) {
         mma_commit(SFULL);  // flush whatever was issued before giving up
@@ -581,21 +751,20 @@ tc_pass2_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
     const float *cp = cst_s + half * kHalf;
     const int k = ct * NC + row;  // this thread's component row of the statistics
     float *dst = partial + ((int64_t)slot * K + k) * PSTRIDE;
-    double lsum = 0.0;
     float nk = 0.0f;
     uint32_t gcount = 0;
     bool ok = true;
     for (int i = 0; i < T && ok; ++i) {
       const int64_t n = (int64_t)(p0 + i) * BM + row;
       const bool valid = n < N;
+      // log2-normalizer and the two exactly re-evaluated components (refine kernel)
       float ln2 = 0.0f;
-      if (valid) {  // merge the pass-1 (max, sum) partials of the component groups
-        float mx = -INFINITY;
-        for (int g = 0; g < G; ++g) mx = fmaxf(mx, __ldg(part_m + (int64_t)g * N + n));
-        float sm = 0.0f;
-        for (int g = 0; g < G; ++g)
-          sm += __ldg(part_s + (int64_t)g * N + n) * ex2(__ldg(part_m + (int64_t)g * N + n) - mx);
-        ln2 = mx + __log2f(sm);
+      int2 ti = make_int2(-1, -1);
+      float2 tl = make_float2(0.0f, 0.0f);
+      if (valid) {
+        ln2 = __ldg(ln2x + n);
+        ti = top_i[n];
+        tl = top_l[n];
       }
       float acc[kHalf];
       ok = drain_group<NB, true>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
@@ -626,10 +795,10 @@ tc_pass2_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
           ++gcount;
         }
       }
-      // the previous tile's statistics leave TMEM before this tile's rounds start
+      // the previous tile's statistics leave TMEM before this tile's round 0 starts
       if (ok && i > 0)
-        ok = drain_stats<NKC>(i - 1, SFULL, SEMPTY, lane_q + kColStats, half, lane,
-                              k < K ? dst : nullptr);
+        ok = drain_stats<NKC, NSR == 2>(i - 1, SFULL, SEMPTY, lane_q + kColStats,
+                                        lane_q + kColStats1, half, lane, k < K ? dst : nullptr);
       ok = epi_sync_and(ok);
       if (!ok) break;
       // Two rounds of 64 points: the round's rows store gamma_hi = tf32(gamma) and
@@ -670,6 +839,22 @@ tc_pass2_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
                   flip ? make_float4(gl[0], gl[1], gl[2], gl[3]) : make_float4(gl[4], gl[5], gl[6], gl[7]);
             }
           }
+          // the exactly re-evaluated leading components replace their tensor-core values
+          const int cb = ct * NC + half * kHalf;
+          const int tix[2] = {ti.x, ti.y};
+          const float tlv[2] = {tl.x, tl.y};
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int lc_ = tix[c] - cb;
+            if (valid && lc_ >= 0 && lc_ < kHalf) {
+              const float g = ex2(tlv[c] - ln2);
+              const float gh = to_tf32(g), gl = to_tf32(g - gh);
+              uint8_t *e = grow + (half * 2 + (lc_ >> 5)) * kGAtom +
+                           ((((lc_ & 31) >> 3) ^ (rp & 3)) << 5) + (lc_ & 7) * 4;
+              *reinterpret_cast<float *>(e) = gh;
+              *reinterpret_cast<float *>(e + kGHalf) = gl;
+            }
+          }
           fence_proxy_async_smem();
         }
         ok = epi_sync_and(ok);  // every row of the round is in place
@@ -692,31 +877,18 @@ tc_pass2_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
         if (!ok) break;
       }
       if (!ok) break;
-      if (ct == 0 && valid && half == 0) {
-        const float l = ln2 * kLn2;
-        ln_out[n] = l;
-        lsum += (double)l;
-      }
     }
     if (ok && T > 0)
-      ok = drain_stats<NKC>(T - 1, SFULL, SEMPTY, lane_q + kColStats, half, lane,
-                            k < K ? dst : nullptr);
+      ok = drain_stats<NKC, NSR == 2>(T - 1, SFULL, SEMPTY, lane_q + kColStats,
+                                      lane_q + kColStats1, half, lane, k < K ? dst : nullptr);
     ok = epi_sync_and(ok);
     if (half == 1) nk_x[row] = nk;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
-    if (lane == 0) lred[warp - 2] = lsum;
     epi_sync_and(true);
     if (k < K) {
       if (!ok || T == 0) {
         for (int f = half * DP; f < (half + 1) * DP; ++f) dst[f] = 0.0f;
       }
       if (half == 0) dst[2 * DP] = (ok && T > 0) ? nk + nk_x[row] : 0.0f;
-    }
-    if (warp == 2 && lane == 0) {
-      double t = 0.0;
-      for (int w = 0; w < kEpiWarps; ++w) t += lred[w];
-      ln_part[blockIdx.x] = t;
     }
   }
   tc_fence_before();
@@ -782,10 +954,15 @@ TcPlan plan(int64_t N, int d, int K) {
 }
 
 struct TcWs {
-  float *qhi, *qlo, *cst2, *part_m, *part_s, *partial;
+  float *qhi, *qlo, *cst2, *sc, *ms, *lc, *part_m, *part_s, *ln2x, *partial;
+  float2 *part_tv, *top_l;
+  int2 *part_ti, *top_i;
   double *ln_part;
   size_t bytes;
 };
+
+constexpr int kRefineBlocks = 8192;  // 32 points per block
+inline int refine_blocks(int64_t N) { return (int)std::min<int64_t>(kRefineBlocks, cdiv(N, 32)); }
 
 TcWs tc_layout(void *ws, const TcPlan &p) {
   TcWs w{};
@@ -793,19 +970,28 @@ TcWs tc_layout(void *ws, const TcPlan &p) {
   w.qhi = c.take<float>((size_t)p.Kp * p.KA);
   w.qlo = c.take<float>((size_t)p.Kp * p.KA);
   w.cst2 = c.take<float>(p.Kp);
+  w.sc = c.take<float>((size_t)p.K * p.d);
+  w.ms = c.take<float>((size_t)p.K * p.d);
+  w.lc = c.take<float>(p.K);
   w.part_m = c.take<float>((size_t)p.G * p.N);
   w.part_s = c.take<float>((size_t)p.G * p.N);
+  w.part_tv = c.take<float2>((size_t)p.G * p.N);
+  w.part_ti = c.take<int2>((size_t)p.G * p.N);
+  w.ln2x = c.take<float>(p.N);
+  w.top_l = c.take<float2>(p.N);
+  w.top_i = c.take<int2>(p.N);
   w.partial = c.take<float>((size_t)p.S * p.K * (2 * p.dp + 4));
-  w.ln_part = c.take<double>(p.grid2);
+  w.ln_part = c.take<double>(kRefineBlocks);
   w.bytes = c.bytes();
   return w;
 }
 
-size_t smem1_bytes() { return 1024 + kStages1 * kStageBytes + 256 + 128 * 8; }
+size_t smem1_bytes() { return 1024 + kStages1 * kStageBytes + 256 + 128 * 24; }
 size_t smem2_bytes() { return 1024 + kStages2 * kStageBytes + kGammaBytes + 1024; }
 
 template <int NKC>
-int tc_launch(const TcPlan &p, const float *pts, const TcWs &w, float *ln, cudaStream_t st) {
+int tc_launch(const TcPlan &p, const float *X, const float *pts, const TcWs &w, float *ln,
+              cudaStream_t st) {
   const float *phi = pts;
   const float *plo = pts + points_half_floats(p.N, p.d);
   const int64_t rows = npad_of(p.N);
@@ -826,12 +1012,30 @@ int tc_launch(const TcPlan &p, const float *pts, const TcWs &w, float *ln, cudaS
     attr_done[NKC / 2] = true;
   }
   tc_pass1_kernel<NKC><<<p.grid1, kThreads, smem1_bytes(), st>>>(
-      m_phi, m_plo, m_qhi, m_qlo, w.cst2, p.N, p.n_pt, p.n_ct, p.G, p.tpg, w.part_m, w.part_s);
+      m_phi, m_plo, m_qhi, m_qlo, w.cst2, p.N, p.n_pt, p.n_ct, p.G, p.tpg, w.part_m, w.part_s,
+      w.part_tv, w.part_ti);
   FGMM_LAUNCH_CHECK("tc_pass1_kernel");
   mark(st, "tc_pass1_kernel");
+  {
+    const int blocks = refine_blocks(p.N);
+    const int dpl = (p.d + 7) / 8;
+#define FGMM_REFINE(D)                                                                          \
+  tc_refine_kernel<D><<<blocks, 256, 0, st>>>(X, p.N, p.d, w.sc, w.ms, w.lc, w.part_m, w.part_s, \
+                                              w.part_tv, w.part_ti, p.G, w.ln2x, w.top_i,       \
+                                              w.top_l, ln, w.ln_part)
+    if (dpl <= 1) FGMM_REFINE(1);
+    else if (dpl <= 2) FGMM_REFINE(2);
+    else if (dpl <= 4) FGMM_REFINE(4);
+    else if (dpl <= 8) FGMM_REFINE(8);
+    else if (dpl <= 12) FGMM_REFINE(12);
+    else FGMM_REFINE(16);
+#undef FGMM_REFINE
+    FGMM_LAUNCH_CHECK("tc_refine_kernel");
+    mark(st, "tc_refine_kernel");
+  }
   tc_pass2_kernel<NKC><<<p.grid2, kThreads, smem2_bytes(), st>>>(
-      m_phi, m_plo, m_phi32, m_plo32, m_qhi, m_qlo, w.cst2, w.part_m, w.part_s, p.N, p.n_pt, p.G,
-      p.S, p.K, w.partial, ln, w.ln_part);
+      m_phi, m_plo, m_phi32, m_plo32, m_qhi, m_qlo, w.cst2, w.ln2x, w.top_i, w.top_l, p.N,
+      p.n_pt, p.S, p.K, w.partial);
   FGMM_LAUNCH_CHECK("tc_pass2_kernel");
   mark(st, "tc_pass2_kernel");
   return FGMM_OK;
@@ -839,7 +1043,7 @@ int tc_launch(const TcPlan &p, const float *pts, const TcWs &w, float *ln, cudaS
 
 }  // namespace
 
-int tc_launches(int64_t, int, int) { return 4; }
+int tc_launches(int64_t, int, int) { return 5; }
 
 bool tc_supported(int64_t N, int d, int K) { return N >= 1 && K >= 1 && d >= 1 && d <= kMaxDp; }
 
@@ -861,23 +1065,24 @@ int tc_prepare_points(const float *X, int64_t N, int d, void *points, cudaStream
 int tc_em_stats(const float *X, const void *points, int64_t N, int d, const float *mu,
                 const float *var, const float *log_pi, int K, double *stats, float *log_norm,
                 void *ws, cudaStream_t st) {
-  (void)X;
   const TcPlan p = plan(N, d, K);
   const TcWs w = tc_layout(ws, p);
-  tc_prep_params_kernel<<<p.Kp, 128, 0, st>>>(mu, var, log_pi, K, d, p.dp, w.qhi, w.qlo, w.cst2);
+  tc_prep_params_kernel<<<p.Kp, 128, 0, st>>>(mu, var, log_pi, K, d, p.dp, w.qhi, w.qlo, w.cst2,
+                                               w.sc, w.ms, w.lc);
   FGMM_LAUNCH_CHECK("tc_prep_params_kernel");
   mark(st, "tc_prep_params_kernel");
   const float *pts = static_cast<const float *>(points);
   int rc;
   switch (p.nkc) {
-    case 2: rc = tc_launch<2>(p, pts, w, log_norm, st); break;
-    case 4: rc = tc_launch<4>(p, pts, w, log_norm, st); break;
-    case 6: rc = tc_launch<6>(p, pts, w, log_norm, st); break;
-    case 8: rc = tc_launch<8>(p, pts, w, log_norm, st); break;
+    case 2: rc = tc_launch<2>(p, X, pts, w, log_norm, st); break;
+    case 4: rc = tc_launch<4>(p, X, pts, w, log_norm, st); break;
+    case 6: rc = tc_launch<6>(p, X, pts, w, log_norm, st); break;
+    case 8: rc = tc_launch<8>(p, X, pts, w, log_norm, st); break;
     default: return fail(FGMM_ERR_UNSUPPORTED, "tcgen05 family: d > 128");
   }
   if (rc) return rc;
-  return reduce_partials(w.partial, p.S, K, d, p.dp, 2 * p.dp + 4, w.ln_part, p.grid2, stats, st);
+  return reduce_partials(w.partial, p.S, K, d, p.dp, 2 * p.dp + 4, w.ln_part, refine_blocks(N), stats,
+                         st);
 }
 
 int tc_device_error(bool reset) {
