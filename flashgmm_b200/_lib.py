@@ -36,6 +36,7 @@ SIGNATURES = {
     "fgmm_em_stats_profiled": (ctypes.c_int, [_vp, _vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _sz, _vp,
                                               ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_char_p), _i32]),
     "fgmm_em_fused_workspace_bytes": (_sz, [_i64, _i32, _i32]),
+    "fgmm_em_fused_static": (ctypes.c_int, [_vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp]),
     "fgmm_em_fused": (ctypes.c_int, [_vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
 }
 

@@ -117,6 +117,25 @@ int fgmm_em_stats_profiled(const float *X, const void *points, int64_t N, int32_
                            void *workspace, size_t workspace_bytes, void *stream,
                            float *launch_ms, const char **names, int32_t n);
 
+/* Size of the fixed device scratch array behind fgmm_em_fused_static. */
+#define FGMM_STATIC_SCRATCH_BYTES (16u << 20)
+
+/* One fused EM iteration (same outputs as fgmm_em_fused, computed by the generic
+ * fp32 CUDA-core kernels) that allocates no device memory, for callers that cannot
+ * call cudaMalloc: code running inside another framework's memory pool, or a process
+ * whose device footprint must stay fixed after start-up.  Its scratch is a fixed
+ * FGMM_STATIC_SCRATCH_BYTES (16 MiB) device array that every GPU loading this library
+ * holds until the process exits; shapes needing more are rejected with
+ * FGMM_ERR_WORKSPACE.  The first call on each device looks up the array's device
+ * address (cudaGetSymbolAddress), so make that first call before any stream capture.
+ * All calls share the array and it keeps the last call's contents: calls that overlap
+ * on the GPU race.  No counterpart in the reference (whose launcher allocates its
+ * scratch with torch on every call). */
+int fgmm_em_fused_static(const float *X, int64_t N, int32_t d,
+                         const float *mu, const float *var, const float *log_pi, int32_t K,
+                         float *new_mu, float *new_var, float *new_log_pi, float *log_normalizer,
+                         void *stream);
+
 #ifdef __cplusplus
 }
 #endif
