@@ -272,13 +272,13 @@ def run_ours(args, wl):
             dist.all_reduce(stats)
         mu, var, lp = C.em_update(stats, n_total, K, d)
 
+    clocks = ClockSampler(gpu_id(dev)).start() if rank == 0 else None
     for _ in range(args.warmup):
         flush.zero_()
         step()
     torch.cuda.synchronize()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
-    clocks = ClockSampler(gpu_id(dev)).start() if rank == 0 else None
     if ws_n > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -324,8 +324,8 @@ def run_ours(args, wl):
     launches = lib.fgmm_em_stats_launches(N, d, K) + 1
     e2e = None
     cpu = None
-    if ws_n == 1 and not args.no_e2e:
-        e2e = run_e2e(wl, dev, args)
+    if not args.no_e2e:
+        e2e = run_e2e(wl, dev, args, ws_n, rank)
     if rank == 0 and ws_n == 1 and not args.no_cpu_baseline:
         s_full, sample, kind, threads = cpu_time_per_iter(wl)
         cpu = {"value": 1.0 / s_full, "unit": "iter/s", "cores": threads, "kind": kind,
@@ -348,39 +348,57 @@ def run_ours(args, wl):
         dist.destroy_process_group()
 
 
-def run_e2e(wl, dev, args):
-    """Whole fits through the public API from pinned host memory: H2D of X and the
-    initial parameters, FIT_ITERS EM iterations, D2H of the fitted parameters."""
-    from flashgmm_b200.native_wrapper import NativeFlashGMM
-    X, mu, var, lp = make_workload(wl)
+def run_e2e(wl, dev, args, ws_n=1, rank=0):
+    """Whole fits through the public API from pinned host memory: H2D of this rank's X
+    shard and the initial parameters, FIT_ITERS EM iterations (NativeFlashGMM on one GPU,
+    DistributedFlashGMM with the stats all_reduce on several), D2H of the fitted
+    parameters.  Wall clock, max over ranks; value counts workload-sized iterations of all
+    ranks per second (weak scaling, like ``value``)."""
+    n_total = wl.N * ws_n
+    X, mu, var, lp = make_workload(wl, N=n_total, rows=(rank * wl.N, (rank + 1) * wl.N))
     Xh = X.pin_memory()
     init_h = [t.pin_memory() for t in (mu, var, lp)]
-    m = NativeFlashGMM(K=wl.K, d=wl.d, max_iter=FIT_ITERS, tol=0.0, device=dev)
+    if ws_n > 1:
+        from flashgmm_b200.distributed import DistributedFlashGMM
+        m = DistributedFlashGMM(K=wl.K, d=wl.d, max_iter=FIT_ITERS, tol=0.0)
+    else:
+        from flashgmm_b200.native_wrapper import NativeFlashGMM
+        m = NativeFlashGMM(K=wl.K, d=wl.d, max_iter=FIT_ITERS, tol=0.0, device=dev)
 
     def one():
         Xd = Xh.to(dev, non_blocking=True)
         init = [t.to(dev, non_blocking=True) for t in init_h]
-        m.fit(Xd, init=init)
+        if ws_n > 1:
+            m.fit(Xd, init)
+        else:
+            m.fit(Xd, init=init)
         return [m.mu.cpu(), m.var.cpu(), m.log_pi.cpu()]
 
     one()
     reps = 3
     torch.cuda.synchronize()
+    if ws_n > 1:
+        dist.barrier()
     t0 = time.perf_counter()
     for _ in range(reps):
         out = one()
     dt = (time.perf_counter() - t0) / reps
+    if ws_n > 1:
+        t = torch.tensor([dt], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = t.item()
     h2d = Xh.numel() * 4 + sum(t.numel() * 4 for t in init_h)
     d2h = sum(t.numel() * 4 for t in out) + 8 * FIT_ITERS
-    return {"value": FIT_ITERS / dt, "unit": "iter/s", "h2d_bytes_per_step": h2d,
+    return {"value": ws_n * FIT_ITERS / dt, "unit": "iter/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
-            "step": f"NativeFlashGMM.fit of {FIT_ITERS} iterations from pinned host X (wall clock)"}
+            "step": (f"{'DistributedFlashGMM' if ws_n > 1 else 'NativeFlashGMM'}.fit of "
+                     f"{FIT_ITERS} iterations from pinned host X (wall clock, per-rank bytes)")}
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="flashgmm", choices=["flashgmm", "reference"])
     ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS))

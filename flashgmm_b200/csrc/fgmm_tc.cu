@@ -447,7 +447,11 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
     float sm = 0.0f;
     for (int g = 0; g < G; ++g)
       sm += __ldg(part_s + (int64_t)g * N + nn) * ex2(__ldg(part_m + (int64_t)g * N + nn) - mx);
+    // the runner-up only matters when it is within 2^-40 of the leader (otherwise its
+    // responsibility is below 1e-12 and its tensor-core value is kept)
+    if (j2 >= 0 && b2 < b1 - 40.0f) j2 = -1;
     const int k1 = j1 >= 0 ? j1 : 0, k2 = j2 >= 0 ? j2 : 0;
+    const bool need2 = __any_sync(0xffffffffu, j2 >= 0);
     float x[DPL], s1[DPL], m1[DPL], s2[DPL], m2[DPL];
 #pragma unroll
     for (int i = 0; i < DPL; ++i) {
@@ -456,8 +460,9 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
       x[i] = in ? __ldg(X + nn * d + j) : 0.0f;
       s1[i] = in ? __ldg(sc + (int64_t)k1 * d + j) : 0.0f;
       m1[i] = in ? __ldg(ms + (int64_t)k1 * d + j) : 0.0f;
-      s2[i] = in ? __ldg(sc + (int64_t)k2 * d + j) : 0.0f;
-      m2[i] = in ? __ldg(ms + (int64_t)k2 * d + j) : 0.0f;
+      const bool in2 = in && need2 && j2 >= 0;
+      s2[i] = in2 ? __ldg(sc + (int64_t)k2 * d + j) : 0.0f;
+      m2[i] = in2 ? __ldg(ms + (int64_t)k2 * d + j) : 0.0f;
     }
     float p1 = 0.0f, p2 = 0.0f;
 #pragma unroll

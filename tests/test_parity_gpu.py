@@ -175,3 +175,33 @@ def test_tail_and_padding_sizes(family):
         ref = oracle.flash_em_fused(X, mu, var, lp, BK=8, nthreads=8)
         g.update(new_mu=ref[0], new_var=ref[1], new_log_pi=ref[2], log_normalizer=ref[3])
         check(f"N={N} K={K} d={d}", got, g, SLACK_BY_FAMILY[family])
+
+
+def test_sharded_class_single_rank_matches_native():
+    """DistributedFlashGMM on one NCCL rank == NativeFlashGMM (same kernels, one no-op
+    all_reduce per iteration)."""
+    import datetime
+    import os
+    import torch.distributed as dist
+    from flashgmm_b200.distributed import DistributedFlashGMM
+    from flashgmm_b200.native_wrapper import NativeFlashGMM
+    g = load_golden("c3_slice4096")
+    dev = torch.device("cuda:0")
+    X = torch.from_numpy(g["X"]).to(dev)
+    init = [torch.from_numpy(g[k]).to(dev) for k in ("mu", "var", "log_pi")]
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29533")
+    created = not dist.is_initialized()
+    if created:
+        dist.init_process_group("nccl", rank=0, world_size=1, device_id=dev,
+                                timeout=datetime.timedelta(seconds=60))
+    try:
+        a = DistributedFlashGMM(init[0].shape[0], X.shape[1], max_iter=5, tol=0.0)
+        ha = a.fit(X, init)
+        b = NativeFlashGMM(init[0].shape[0], X.shape[1], max_iter=5, tol=0.0)
+        hb = b.fit(X, init=init)
+        assert torch.equal(a.mu, b.mu) and torch.equal(a.var, b.var) and torch.equal(a.log_pi, b.log_pi)
+        assert [h["log_likelihood"] for h in ha] == [h["log_likelihood"] for h in hb]
+    finally:
+        if created:
+            dist.destroy_process_group()
