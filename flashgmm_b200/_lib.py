@@ -9,7 +9,7 @@ import ctypes
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libflashgmm_b200.so")
+LIB_PATH = os.environ.get("FLASHGMM_LIB") or os.path.join(HERE, "libflashgmm_b200.so")
 
 FGMM_OK = 0
 FGMM_ERR_INVALID = 1

@@ -167,13 +167,25 @@ __device__ __forceinline__ bool epi_sync_and(bool v) {
 // with the small terms summed first, added on the CUDA cores, match a direct fp32
 // evaluation of the Mahalanobis sum.
 
-// MMA side: one staged 32-column chunk = one group, rotating over NB TMEM buffers.
+// K group size in staged 32-column chunks (divides NKC).
+#ifndef FGMM_GROUP_CHUNKS
+#define FGMM_GROUP_CHUNKS 1
+#endif
+template <int NKC>
+__host__ __device__ constexpr int group_chunks() {
+  constexpr int g = FGMM_GROUP_CHUNKS < NKC ? FGMM_GROUP_CHUNKS : NKC;
+  return NKC % g == 0 ? g : (NKC % 2 == 0 ? 2 : 1);
+}
+
+// MMA side: one staged 32-column chunk of a K group that rotates over NB TMEM buffers;
+// gfirst / glast mark the group's first / last chunk.
 template <int NB>
 __device__ __forceinline__ bool issue_dist_chunk(uint32_t base, uint32_t tmem, uint32_t &gcount,
-                                                 uint32_t tfull0, uint32_t tempty0) {
+                                                 uint32_t tfull0, uint32_t tempty0, bool gfirst,
+                                                 bool glast) {
   constexpr uint32_t idesc = idesc_tf32(BM, NC, 0, 0);
   const uint32_t buf = gcount % NB, use = gcount / NB;
-  if (!mbar_wait(tempty0 + 8u * buf, (use & 1u) ^ 1u, kErrWaitTmemEmpty)) return false;
+  if (gfirst && !mbar_wait(tempty0 + 8u * buf, (use & 1u) ^ 1u, kErrWaitTmemEmpty)) return false;
   tc_fence_after();
   const uint32_t d = tmem + buf * NC;
 #pragma unroll
@@ -182,7 +194,7 @@ __device__ __forceinline__ bool issue_dist_chunk(uint32_t base, uint32_t tmem, u
     const uint64_t al = sdesc_sw128(base + kTileBytes + kk * 32, 16, 1024);
     const uint64_t bh = sdesc_sw128(base + 2 * kTileBytes + kk * 32, 16, 1024);
     const uint64_t bl = sdesc_sw128(base + 3 * kTileBytes + kk * 32, 16, 1024);
-    mma_tf32(d, al, bh, idesc, kk != 0 ? 1u : 0u);
+    mma_tf32(d, al, bh, idesc, (kk != 0 || !gfirst) ? 1u : 0u);
     mma_tf32(d, ah, bl, idesc, 1u);
   }
 #pragma unroll
@@ -191,8 +203,10 @@ __device__ __forceinline__ bool issue_dist_chunk(uint32_t base, uint32_t tmem, u
     const uint64_t bh = sdesc_sw128(base + 2 * kTileBytes + kk * 32, 16, 1024);
     mma_tf32(d, ah, bh, idesc, 1u);
   }
-  mma_commit(tfull0 + 8u * buf);
-  ++gcount;
+  if (glast) {
+    mma_commit(tfull0 + 8u * buf);
+    ++gcount;
+  }
   return true;
 }
 
@@ -303,8 +317,9 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
           for (int c = 0; c < NKC; ++c) {
             if (!mbar_wait(FULL(stage), phase, kErrWaitFull)) { ok = false; break; }
             tc_fence_after();
+            constexpr int GC = group_chunks<NKC>();
             if (!issue_dist_chunk<NB>(smem_u32(smem + stage * kStageBytes), tmem, gcount, TFULL0,
-                                      TEMPTY0)) { ok = false; break; }
+                                      TEMPTY0, c % GC == 0, c % GC == GC - 1)) { ok = false; break; }
             mma_commit(EMPTY(stage));
             if (++stage == S) { stage = 0; phase ^= 1; }
           }
@@ -330,7 +345,7 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
         float acc[kHalf];
         ok = drain_group<NB, true>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
 #pragma unroll 1
-        for (int grp = 1; grp < NKC && ok; ++grp)
+        for (int grp = 1; grp < NKC / group_chunks<NKC>() && ok; ++grp)
           ok = drain_group<NB, false>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
         if (!ok) break;
         const float *cp = cst2 + (int64_t)t * NC + half * kHalf;
@@ -680,8 +695,9 @@ tc_pass2_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
         for (int c = c0; c < c1 && ok; ++c) {
           if (!mbar_wait(FULL(stage), phase, kErrWaitFull)) { ok = false; return; }
           tc_fence_after();
+          constexpr int GC = group_chunks<NKC>();
           if (!issue_dist_chunk<NB>(smem_u32(smem + stage * kStageBytes), tmem, gcount, TFULL0,
-                                    TEMPTY0)) { ok = false; return; }
+                                    TEMPTY0, c % GC == 0, c % GC == GC - 1)) { ok = false; return; }
           mma_commit(EMPTY(stage));
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
@@ -771,11 +787,17 @@ tc_pass2_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
         ti = top_i[n];
         tl = top_l[n];
       }
+      constexpr int GPT = NKC / group_chunks<NKC>();  // K groups per tile
       float acc[kHalf];
-      ok = drain_group<NB, true>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
+      if constexpr (GPT > 1) {
+        ok = drain_group<NB, true>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
 #pragma unroll 1
-      for (int grp = 1; grp < NKC - 1 && ok; ++grp)
-        ok = drain_group<NB, false>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
+        for (int grp = 1; grp < GPT - 1 && ok; ++grp)
+          ok = drain_group<NB, false>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
+      } else {
+#pragma unroll
+        for (int e = 0; e < kHalf; ++e) acc[e] = 0.0f;
+      }
       // The last K group is drained straight into gamma = 2^(l2 - ln2) (fp32, in acc).
       if (ok) {
         const uint32_t buf = gcount % NB, use = gcount / NB;
