@@ -50,14 +50,8 @@ constexpr int kThreads = 64 + 32 * kEpiWarps; // warp 0 TMA, warp 1 MMA, warps 2
 constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kHalf = 64;                     // columns of a tile owned by one epilogue warp
 constexpr int kStages1 = 3;
-constexpr int kStages2 = 2;
 constexpr int kTileBytes = BM * KC * 4;       // 16 KB: 128 rows x 128 B
 constexpr int kStageBytes = 4 * kTileBytes;   // 64 KB
-constexpr int kSubBytes = 32 * KC * 4;        // 4 KB: 32 rows x 128 B
-constexpr int kGammaBytes = NC * BM * 4;      // 64 KB: gamma_hi and gamma_lo of 64 points
-constexpr int kRoundPts = 64;                 // points of a tile staged per gamma round
-constexpr int kGHalf = kGammaBytes / 2;       // 32 KB: one of gamma_hi / gamma_lo
-constexpr int kGAtom = kRoundPts * 128;       // 8 KB: 32 components x 64 points
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int kMaxDp = 128;                   // d <= 128 runs here
@@ -241,7 +235,8 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
                 const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant__ CUtensorMap tm_qlo,
                 const float *__restrict__ cst2, int64_t N, int n_pt, int n_ct, int G, int tpg,
                 float *__restrict__ part_m, float *__restrict__ part_s,
-                float2 *__restrict__ part_tv, int2 *__restrict__ part_ti) {
+                float2 *__restrict__ part_tv, int2 *__restrict__ part_ti,
+                float *__restrict__ Lout, int Kp) {
   constexpr int S = kStages1;
   constexpr int NB = 4;  // TMEM group buffers (4 x 128 columns)
   extern __shared__ uint8_t smem_raw[];
@@ -341,6 +336,7 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
       float m = -INFINITY, s = 0.0f;
       float v1 = -INFINITY, v2 = -INFINITY;  // the row's two largest log2-likelihoods
       int i1 = -1, i2 = -1;
+      const int64_t n_row = (int64_t)pt * BM + row;
       for (int t = g * tpg; t < t1 && ok; ++t) {
         float acc[kHalf];
         ok = drain_group<NB, true>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
@@ -356,6 +352,13 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
           for (int e = 0; e < 32; ++e) {
             acc[j * 32 + e] = fmaf(acc[j * 32 + e], -0.5f * kLog2e, __ldg(cp + j * 32 + e));
             cm = fmaxf(cm, acc[j * 32 + e]);
+          }
+          if (n_row < N) {  // the log2-likelihood matrix L feeds the statistics pass
+            float4 *lp = reinterpret_cast<float4 *>(Lout + n_row * Kp + t * NC + half * kHalf + j * 32);
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              lp[e] = make_float4(acc[j * 32 + 4 * e], acc[j * 32 + 4 * e + 1],
+                                  acc[j * 32 + 4 * e + 2], acc[j * 32 + 4 * e + 3]);
           }
           const float mn = fmaxf(m, cm);
           const float mr = (mn == -INFINITY) ? 0.0f : mn;
@@ -524,403 +527,274 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
 }
 
 // ------------------------------------------------------------------------- pass 2
-// Add (or, for the CTA's first tile j == 0, store) the TMEM statistics of tile j into the CTA's
-// partial row `dst` ([s (DP) | sq (DP) | n | pad]); warp half 0 takes the x^2 features
-// (-> sq), half 1 the x features (-> s).  dst == nullptr: padding component, no store.
-template <int NKC, bool kTwo>
-__device__ __forceinline__ bool drain_stats(int j, uint32_t sfull, uint32_t sempty,
-                                            uint32_t stats_tmem, uint32_t stats_tmem1, int half,
-                                            int lane, float *dst) {
-  constexpr int DP = NKC * KC / 2;
-  if (!__all_sync(0xffffffffu, mbar_wait(sfull, j & 1, kErrWaitStatsDone))) return false;
-  tc_fence_after();
-#pragma unroll 1
-  for (int c = half * (NKC / 2); c < (half + 1) * (NKC / 2); ++c) {
-    float v[32];
-    tmem_ld32(stats_tmem + c * 32, v);
-    tmem_wait_ld();
-    if (kTwo) {
-      float w[32];
-      tmem_ld32(stats_tmem1 + c * 32, w);
-      tmem_wait_ld();
-#pragma unroll
-      for (int e = 0; e < 32; ++e) v[e] += w[e];
-    }
-    if (dst) {
-      float *o = dst + (half == 0 ? DP + c * 32 : c * 32 - DP);
-#pragma unroll
-      for (int e = 0; e < 32; e += 4) {
-        const float4 w = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
-        if (j > 0) red_add_v4(o + e, w);  // same-thread store/reds to one address stay ordered
-        else *reinterpret_cast<float4 *>(o + e) = w;
-      }
-    }
-  }
-  tc_fence_before();
-  __syncwarp();
-  if (lane == 0) mbar_arrive(sempty);
-  return true;
+// Statistics GEMM S[k, f] = sum_n gamma[n, k] F[n, f] with F = [x^2 | x] (3xTF32), the
+// only tensor-core work left once pass 1 has stored the log2-likelihood matrix L.
+// A CTA owns 128 components (the M of the MMA) and a contiguous range of points, taken
+// in rounds of 32 points (the K of four MMA k-steps).  Its sixteen warps build each
+// round's operands straight from global memory: gamma = 2^(L - ln2) with the two
+// refined components replaced by their exact values, and F from X, both split into
+// tf32 hi/lo in the MN-major SWIZZLE_128B_BASE32B layout, double-buffered; after a
+// barrier one thread issues the round's MMAs.  The accumulator alternates between two
+// TMEM regions every kRoundsFlush rounds; while the tensor pipe fills one region the
+// warps add the other into fp32 registers, so tensor-memory accumulation (not
+// round-to-nearest) never spans more than 128 points and the running sums stay on chip
+// until the CTA ends.
+constexpr int kRoundPts2 = 32;
+constexpr int kRoundsFlush = 4;
+constexpr int kWorkWarps = 16;
+constexpr int kThreads2 = 32 * kWorkWarps;
+constexpr int kAtom2 = kRoundPts2 * 128;         // 4 KB: 32 points x 32 fp32
+constexpr int kGOff2 = 0, kGLoOff2 = 4 * kAtom2;  // gamma^T hi / lo: 4 component atoms each
+constexpr int kFOff2 = 8 * kAtom2;                // F hi: up to 8 feature atoms
+constexpr int kFLoOff2 = kFOff2 + 8 * kAtom2;     // F lo
+constexpr int kBuf2 = kFLoOff2 + 8 * kAtom2;      // 96 KB per round buffer
+
+__device__ __forceinline__ bool cta_sync_and(bool v) {
+  return __syncthreads_and(v ? 1 : 0) != 0;
 }
+
+// Stores 8 consecutive fp32 (one 32-byte chunk of a 128-byte MN-major row) as hi and lo
+// tf32 parts.  The two 16-byte halves are stored in an order that alternates between odd
+// and even atoms, so a warp's stores (16 chunks of 2 rows over 4 atoms) hit every bank once
+// per 128 bytes.
+__device__ __forceinline__ void put_chunk8(uint8_t *hi, uint8_t *lo, const float (&v)[8], int flip) {
+  float h[8], l[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    h[e] = to_tf32(v[e]);
+    l[e] = to_tf32(v[e] - h[e]);
+  }
+  const float4 h0 = make_float4(h[0], h[1], h[2], h[3]), h1 = make_float4(h[4], h[5], h[6], h[7]);
+  const float4 l0 = make_float4(l[0], l[1], l[2], l[3]), l1 = make_float4(l[4], l[5], l[6], l[7]);
+  const int o0 = flip << 4, o1 = (flip ^ 1) << 4;  // store order only; data stays in place
+  *reinterpret_cast<float4 *>(hi + o0) = flip ? h1 : h0;
+  *reinterpret_cast<float4 *>(hi + o1) = flip ? h0 : h1;
+  *reinterpret_cast<float4 *>(lo + o0) = flip ? l1 : l0;
+  *reinterpret_cast<float4 *>(lo + o1) = flip ? l0 : l1;
+}
+
+// Inputs one thread needs for one round (prefetched a round ahead).
+struct RoundIn {
+  float l[8];   // log2-likelihoods of the thread's 8 components at its point
+  float x[8];   // 8 coordinates of the thread's feature chunk
+  float ln2;    // the point's log2-normalizer
+  int2 ti;      // its two refined components
+  float2 tl;    // and their exact log2-likelihoods
+};
 
 // Partial statistics row (per CTA slot and component): [s (DP) | sq (DP) | n | pad],
 // stride 2 DP + 4.
 template <int NKC>
-__global__ void __launch_bounds__(kThreads, 1)
-tc_pass2_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ CUtensorMap tm_plo,
-                const __grid_constant__ CUtensorMap tm_phi32, const __grid_constant__ CUtensorMap tm_plo32,
-                const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant__ CUtensorMap tm_qlo,
-                const float *__restrict__ cst2, const float *__restrict__ ln2x,
-                const int2 *__restrict__ top_i, const float2 *__restrict__ top_l, int64_t N,
-                int n_pt, int S_slots, int K, float *__restrict__ partial) {
-  constexpr int S = kStages2;
+__global__ void __launch_bounds__(kThreads2, 1)
+tc_stats_kernel(const float *__restrict__ X, int d, int x_vec, const float *__restrict__ L,
+                int Kp, const float *__restrict__ ln2x, const int2 *__restrict__ top_i,
+                const float2 *__restrict__ top_l, int64_t N, int S_slots, int K,
+                float *__restrict__ partial) {
   constexpr int KA = NKC * KC;
   constexpr int DP = KA / 2;
   constexpr int PSTRIDE = 2 * DP + 4;
-  // For KA <= 128 TMEM holds two statistics regions: rounds 0 and 1 accumulate
-  // separately (half the additions each, at half the magnitude) and the drain adds them
-  // in fp32.
-  constexpr int NSR = KA <= 128 ? 2 : 1;
-  constexpr int NB = (512 - NSR * KA) / NC;  // TMEM group buffers for the distance GEMM
-  constexpr uint32_t kColStats = NB * NC;    // TMEM column of S[k, f] (round 0 region)
-  constexpr uint32_t kColStats1 = kColStats + (NSR == 2 ? KA : 0);  // round 1 region
-  // Per tile the MMA issues the first NP distance groups of the next tile, statistics
-  // round 0 of this tile, the rest of the next tile, statistics round 1 (the producer
-  // loads in the same order): no round waits behind distance groups whose TMEM buffers
-  // only the next epilogue iteration frees, and the tensor pipe has distance work while
-  // the epilogue prepares round 1.
-  constexpr int NP = NB < NKC ? NB : NKC;
-  static_assert(NB >= 2, "TMEM budget");
+  constexpr int SEG = KA / 4;  // statistics columns per thread
+  constexpr int FCH = DP / 8;  // 8-feature chunks per point
+  static_assert(2 * KA <= 512, "two statistics regions must fit in TMEM");
+  static_assert(SEG % 16 == 0, "statistics segment of whole 16-column loads");
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = align1024(smem_raw);
-  uint8_t *gamma = smem + S * kStageBytes;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(gamma + kGammaBytes);
-  // bars: full[S] empty[S] tfull[NB] tempty[NB] gfull gempty sfull sempty
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 2 * NB + 4);
-  double *lred = reinterpret_cast<double *>(bars + 2 * S + 2 * NB + 5);  // [kEpiWarps]
-  float *nk_x = reinterpret_cast<float *>(lred + kEpiWarps);              // [128]
-  float *cst_s = nk_x + NC;                                                // [128] cst2 of this tile
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 2 * kBuf2);
+  // bars: gempty[2] sfull[2] done
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 5);
   const uint32_t bar0 = smem_u32(bars);
-  auto FULL = [&](int s) { return bar0 + 8u * s; };
-  auto EMPTY = [&](int s) { return bar0 + 8u * (S + s); };
-  const uint32_t TFULL0 = bar0 + 8u * (2 * S), TEMPTY0 = bar0 + 8u * (2 * S + NB);
-  const uint32_t GFULL = bar0 + 8u * (2 * S + 2 * NB), GEMPTY = GFULL + 8;
-  const uint32_t SFULL = GFULL + 16, SEMPTY = GFULL + 24;
+  auto GEMPTY = [&](int b) { return bar0 + 8u * b; };
+  auto SFULL = [&](int b) { return bar0 + 8u * (2 + b); };
+  const uint32_t DONE = bar0 + 8u * 4;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wt = threadIdx.x;
   const int ct = blockIdx.x / S_slots, slot = blockIdx.x % S_slots;
-  const int p0 = (int)((int64_t)slot * n_pt / S_slots);
-  const int p1 = (int)((int64_t)(slot + 1) * n_pt / S_slots);
-  const int T = p1 - p0;
+  const int64_t n_rounds = (N + kRoundPts2 - 1) / kRoundPts2;
+  const int64_t r0 = slot * n_rounds / S_slots, r1 = (slot + 1) * n_rounds / S_slots;
+  const int R = (int)(r1 - r0);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) { mbar_init(FULL(s), 1); mbar_init(EMPTY(s), 1); }
-    for (int b = 0; b < NB; ++b) {
-      mbar_init(TFULL0 + 8u * b, 1);
-      mbar_init(TEMPTY0 + 8u * b, kEpiWarps);
-    }
-    mbar_init(GFULL, kEpiWarps); mbar_init(GEMPTY, 1);
-    mbar_init(SFULL, 1); mbar_init(SEMPTY, kEpiWarps);
+    for (int b = 0; b < 2; ++b) { mbar_init(GEMPTY(b), 1); mbar_init(SFULL(b), 1); }
+    mbar_init(DONE, 1);
     fence_mbar_init();
   }
-  if (warp == 1) {
+  if (warp == 0) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
-  if (threadIdx.x >= 64 && threadIdx.x < 64 + NC)
-    cst_s[threadIdx.x - 64] = cst2[(int64_t)ct * NC + threadIdx.x - 64];
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    if (lane == 0 && T > 0) {
-      prefetch_tmap(&tm_phi); prefetch_tmap(&tm_plo); prefetch_tmap(&tm_phi32);
-      prefetch_tmap(&tm_plo32); prefetch_tmap(&tm_qhi); prefetch_tmap(&tm_qlo);
-      int stage = 0;
-      uint32_t phase = 0, armed = 0, armed_par = 0;
-      bool ok = true;
-      auto acquire = [&]() -> uint32_t {
-        if (!mbar_wait(EMPTY(stage), phase ^ 1, kErrWaitEmpty)) { ok = false; return 0; }
-        return smem_u32(smem + stage * kStageBytes);
-      };
-      auto advance = [&]() {
-        armed |= 1u << stage;
-        armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
-        if (++stage == S) { stage = 0; phase ^= 1; }
-      };
-      auto load_dist = [&](int pt, int c0, int c1) {
-        for (int c = c0; c < c1 && ok; ++c) {
-          const uint32_t base = acquire();
-          if (!ok) return;
-          mbar_arrive_expect_tx(FULL(stage), kStageBytes);
-          tma_load_2d(base, &tm_phi, c * KC, pt * BM, FULL(stage));
-          tma_load_2d(base + kTileBytes, &tm_plo, c * KC, pt * BM, FULL(stage));
-          tma_load_2d(base + 2 * kTileBytes, &tm_qhi, c * KC, ct * NC, FULL(stage));
-          tma_load_2d(base + 3 * kTileBytes, &tm_qlo, c * KC, ct * NC, FULL(stage));
-          advance();
-        }
-      };
-      auto load_stats = [&](int pt, int r) {
-        for (int sub = 2 * r; sub < 2 * r + 2 && ok; ++sub) {
-          const uint32_t base = acquire();
-          if (!ok) return;
-          mbar_arrive_expect_tx(FULL(stage), 2 * NKC * kSubBytes);
-          for (int c = 0; c < NKC; ++c) {
-            tma_load_2d(base + c * kSubBytes, &tm_phi32, c * KC, pt * BM + sub * 32, FULL(stage));
-            tma_load_2d(base + (NKC + c) * kSubBytes, &tm_plo32, c * KC, pt * BM + sub * 32,
-                        FULL(stage));
-          }
-          advance();
-        }
-      };
-      load_dist(p0, 0, NKC);
-      for (int i = 0; i < T && ok; ++i) {
-        if (i + 1 < T) load_dist(p0 + i + 1, 0, NP);
-        load_stats(p0 + i, 0);
-        if (i + 1 < T) load_dist(p0 + i + 1, NP, NKC);
-        load_stats(p0 + i, 1);
-      }
-      for (int s = 0; s < S; ++s)
-        if (armed & (1u << s)) mbar_wait(FULL(s), (armed_par >> s) & 1u, kErrWaitDrain);
+  const int q = warp & 3, seg = warp >> 2;  // TMEM lane quarter, column segment
+  const uint32_t lane_tmem = tmem + ((uint32_t)(q * 32) << 16) + seg * SEG;
+  // gamma role: point pr of the round, components cg*8 .. cg*8+7 of this CTA's 128
+  const int pr = wt >> 4, cg = wt & 15;
+  const int ga = cg >> 2, gc8 = cg & 3;
+  const int kb = ct * NC + cg * 8;
+  // feature role: point fp, feature chunk fc (the first 32 * FCH threads)
+  const bool f_on = wt < kRoundPts2 * FCH;
+  const int fp = wt / FCH, fc = wt % FCH;
+  const int fa = fc >> 2, fc8 = fc & 3;
+  float sacc[SEG];
+#pragma unroll
+  for (int e = 0; e < SEG; ++e) sacc[e] = 0.0f;
+  float nk[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) nk[e] = 0.0f;
+
+  auto fetch = [&](int r, RoundIn &in) {
+    const int64_t nb = (r0 + r) * kRoundPts2;
+    const int64_t n = nb + pr;
+    if (n < N) {
+      const float4 *lp = reinterpret_cast<const float4 *>(L + n * Kp + kb);
+      const float4 a = __ldg(lp), c = __ldg(lp + 1);
+      in.l[0] = a.x; in.l[1] = a.y; in.l[2] = a.z; in.l[3] = a.w;
+      in.l[4] = c.x; in.l[5] = c.y; in.l[6] = c.z; in.l[7] = c.w;
+      in.ln2 = __ldg(ln2x + n);
+      in.ti = top_i[n];
+      in.tl = top_l[n];
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) in.l[e] = -INFINITY;
+      in.ln2 = 0.0f;
+      in.ti = make_int2(-1, -1);
+      in.tl = make_float2(0.0f, 0.0f);
     }
-  } else if (warp == 1) {
-    if (lane == 0 && T > 0) {
-      constexpr uint32_t idesc_s = idesc_tf32(NC, KA, 1, 1);  // stats: MN-major A and B
-      const uint32_t gbase = smem_u32(gamma);
-      int stage = 0;
-      uint32_t phase = 0, gcount = 0;
-      bool ok = true;
-      auto issue_dist = [&](int c0, int c1) {
-        for (int c = c0; c < c1 && ok; ++c) {
-          if (!mbar_wait(FULL(stage), phase, kErrWaitFull)) { ok = false; return; }
-          tc_fence_after();
-          constexpr int GC = group_chunks<NKC>();
-          if (!issue_dist_chunk<NB>(smem_u32(smem + stage * kStageBytes), tmem, gcount, TFULL0,
-                                    TEMPTY0, c % GC == 0, c % GC == GC - 1)) { ok = false; return; }
-          mma_commit(EMPTY(stage));
-          if (++stage == S) { stage = 0; phase ^= 1; }
-        }
-      };
-      // Statistics round r of tile i: 64 points in two staged 32-point sub-chunks.  The
-      // TMEM statistics restart every tile (the epilogue flushes them after round 1), and
-      // within a round all small products (gamma_lo.F_hi, gamma_hi.F_lo) go before the
-      // gamma_hi.F_hi ones, which keeps additions at the accumulator's full magnitude few.
-      auto issue_round = [&](int i, int r) {
-        const uint32_t rc = 2u * i + r;
-        if (!mbar_wait(GFULL, rc & 1u, kErrWaitGammaFull)) { ok = false; return; }
-        if (r == 0 && i > 0 && !mbar_wait(SEMPTY, (i - 1) & 1u, kErrWaitStatsDone)) {
-          ok = false;
-          return;
-        }
-        uint32_t base[2];
-        int st[2];
-        for (int s2 = 0; s2 < 2; ++s2) {
-          if (!mbar_wait(FULL(stage), phase, kErrWaitFull)) { ok = false; return; }
-          base[s2] = smem_u32(smem + stage * kStageBytes);
-          st[s2] = stage;
-          if (++stage == S) { stage = 0; phase ^= 1; }
-        }
-        tc_fence_after();
-        const uint32_t dstat = tmem + (r == 0 ? kColStats : kColStats1);
-        const uint32_t first = NSR == 2 ? 0u : (uint32_t)r;  // round restarts its region
-        // gamma^T: MN-major (components contiguous), 4-point atoms of 512 B, component
-        // atoms 8 KB apart; F: MN-major (features contiguous), 4 KB per 32 features.
+    const int64_t m = nb + fp;
+    const int j0 = fc * 8;
+    if (f_on && m < N && x_vec && j0 + 8 <= d) {
+      const float4 *xp = reinterpret_cast<const float4 *>(X + m * d + j0);
+      const float4 a = __ldg(xp), c = __ldg(xp + 1);
+      in.x[0] = a.x; in.x[1] = a.y; in.x[2] = a.z; in.x[3] = a.w;
+      in.x[4] = c.x; in.x[5] = c.y; in.x[6] = c.z; in.x[7] = c.w;
+    } else {
 #pragma unroll
-        for (int s2 = 0; s2 < 2; ++s2)
+      for (int e = 0; e < 8; ++e)
+        in.x[e] = (f_on && m < N && j0 + e < d) ? __ldg(X + m * d + j0 + e) : 0.0f;
+    }
+  };
+  // Adds TMEM region j & 1 (flush tile j) into sacc.
+  auto flush = [&](int j) -> bool {
+    const int sb = j & 1;
+    if (!__all_sync(0xffffffffu, mbar_wait(SFULL(sb), (j >> 1) & 1, kErrWaitStatsDone)))
+      return false;
+    tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t ga = gbase + (s2 * 4 + kk) * 1024;
-            const uint64_t ah = sdesc(ga, kGAtom, 512, kSw128Base32);
-            const uint64_t al = sdesc(ga + kGHalf, kGAtom, 512, kSw128Base32);
-            const uint64_t fh = sdesc(base[s2] + kk * 1024, kSubBytes, 512, kSw128Base32);
-            const uint64_t fl = sdesc(base[s2] + NKC * kSubBytes + kk * 1024, kSubBytes, 512, kSw128Base32);
-            mma_tf32(dstat, al, fh, idesc_s, (first | s2 | kk) ? 1u : 0u);
-            mma_tf32(dstat, ah, fl, idesc_s, 1u);
-          }
+    for (int c = 0; c < SEG / 16; ++c) {
+      float v[16];
+      tmem_ld16(lane_tmem + sb * KA + c * 16, v);
+      tmem_wait_ld();
 #pragma unroll
-        for (int s2 = 0; s2 < 2; ++s2)
+      for (int e = 0; e < 16; ++e) sacc[c * 16 + e] += v[e];
+    }
+    tc_fence_before();
+    return true;
+  };
+
+  bool ok = true;
+  RoundIn nxt;
+  if (R > 0) fetch(0, nxt);
+  for (int r = 0; r < R; ++r) {
+    const RoundIn cur = nxt;
+    if (r + 1 < R) fetch(r + 1, nxt);
+    const int b = r & 1;
+    // buffer b is free once the MMAs of round r - 2 have read it
+    ok = __all_sync(0xffffffffu, mbar_wait(GEMPTY(b), ((r >> 1) & 1) ^ 1, kErrWaitGammaEmpty));
+    if (ok) {
+      uint8_t *buf = smem + b * kBuf2;
+      float g[8];
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t ah = sdesc(gbase + (s2 * 4 + kk) * 1024, kGAtom, 512, kSw128Base32);
-            const uint64_t fh = sdesc(base[s2] + kk * 1024, kSubBytes, 512, kSw128Base32);
-            mma_tf32(dstat, ah, fh, idesc_s, 1u);
-          }
-        mma_commit(EMPTY(st[0]));
-        mma_commit(EMPTY(st[1]));
-        mma_commit(GEMPTY);
-        if (r == 1) mma_commit(SFULL);
-      };
-      issue_dist(0, NKC);
-      for (int i = 0; i < T && ok; ++i) {
-        if (i + 1 < T) issue_dist(0, NP);
-        if (ok) issue_round(i, 0);
-        if (ok && i + 1 < T) issue_dist(NP, NKC);
-        if (ok) issue_round(i, 1);
+      for (int e = 0; e < 8; ++e) {
+        float l2 = cur.l[e];
+        if (kb + e == cur.ti.x) l2 = cur.tl.x;
+        if (kb + e == cur.ti.y) l2 = cur.tl.y;
+        g[e] = ex2(l2 - cur.ln2);
+        nk[e] += g[e];
       }
-      if (!ok) {
-        mma_commit(SFULL);  // flush whatever was issued before giving up
-        mbar_wait(SFULL, 0, kErrWaitDrain);
+      uint8_t *grow = buf + ga * kAtom2 + pr * 128 + ((gc8 ^ (pr & 3)) << 5);
+      put_chunk8(grow + kGOff2, grow + kGLoOff2, g, ga & 1);
+      if (f_on) {
+        float x2[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x2[e] = cur.x[e] * cur.x[e];
+        uint8_t *frow = buf + fa * kAtom2 + fp * 128 + ((fc8 ^ (fp & 3)) << 5);
+        put_chunk8(frow + kFOff2, frow + kFLoOff2, x2, fa & 1);
+        frow += (DP / 32) * kAtom2;
+        put_chunk8(frow + kFOff2, frow + kFLoOff2, cur.x, fa & 1);
       }
+      fence_proxy_async_smem();
+    }
+    // every operand of the round is in place, and every flush issued so far is done
+    ok = cta_sync_and(ok);
+    if (!ok) break;
+    const int j = r / kRoundsFlush, sb = j & 1;
+    if (wt == 0) {
+      constexpr uint32_t idesc = idesc_tf32(NC, KA, 1, 1);  // both operands MN-major
+      tc_fence_after();
+      const uint32_t base = smem_u32(smem + b * kBuf2);
+      const uint32_t dst = tmem + sb * KA;
+      const bool tile_first = r % kRoundsFlush == 0;
+      // small products (gamma_lo F_hi, gamma_hi F_lo) before gamma_hi F_hi
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint64_t gh = sdesc(base + kGOff2 + kk * 1024, kAtom2, 512, kSw128Base32);
+        const uint64_t gl = sdesc(base + kGLoOff2 + kk * 1024, kAtom2, 512, kSw128Base32);
+        const uint64_t fh = sdesc(base + kFOff2 + kk * 1024, kAtom2, 512, kSw128Base32);
+        const uint64_t fl = sdesc(base + kFLoOff2 + kk * 1024, kAtom2, 512, kSw128Base32);
+        mma_tf32(dst, gl, fh, idesc, (tile_first && kk == 0) ? 0u : 1u);
+        mma_tf32(dst, gh, fl, idesc, 1u);
+      }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint64_t gh = sdesc(base + kGOff2 + kk * 1024, kAtom2, 512, kSw128Base32);
+        const uint64_t fh = sdesc(base + kFOff2 + kk * 1024, kAtom2, 512, kSw128Base32);
+        mma_tf32(dst, gh, fh, idesc, 1u);
+      }
+      mma_commit(GEMPTY(b));
+      if (r % kRoundsFlush == kRoundsFlush - 1 || r == R - 1) mma_commit(SFULL(sb));
     }
     __syncwarp();
-  } else {
-    const int q = warp & 3, half = (warp - 2) >> 2;
-    const int row = q * 32 + lane;
-    const uint32_t lane_q = tmem + ((uint32_t)(q * 32) << 16);
-    const uint32_t lane_tmem = lane_q + half * kHalf;
-    const float *cp = cst_s + half * kHalf;
-    const int k = ct * NC + row;  // this thread's component row of the statistics
+    // The previous tile's region is added into registers once this tile's first round
+    // is queued; the barrier of the next round orders it before that region's reuse
+    // (two tiles later, kRoundsFlush >= 2 rounds on).
+    if (r % kRoundsFlush == 0 && r > 0) ok = flush(j - 1);
+  }
+  if (ok && R > 0) ok = flush((R - 1) / kRoundsFlush);
+  // no MMA of this CTA may still run at the teardown (also after an early exit)
+  if (wt == 0 && R > 0) {
+    mma_commit(DONE);
+    mbar_wait(DONE, 0, kErrWaitDrain);
+  }
+  ok = cta_sync_and(ok);
+  const int k = ct * NC + q * 32 + lane;  // TMEM lane = component
+  if (k < K) {
     float *dst = partial + ((int64_t)slot * K + k) * PSTRIDE;
-    float nk = 0.0f;
-    uint32_t gcount = 0;
-    bool ok = true;
-    for (int i = 0; i < T && ok; ++i) {
-      const int64_t n = (int64_t)(p0 + i) * BM + row;
-      const bool valid = n < N;
-      // log2-normalizer and the two exactly re-evaluated components (refine kernel)
-      float ln2 = 0.0f;
-      int2 ti = make_int2(-1, -1);
-      float2 tl = make_float2(0.0f, 0.0f);
-      if (valid) {
-        ln2 = __ldg(ln2x + n);
-        ti = top_i[n];
-        tl = top_l[n];
-      }
-      constexpr int GPT = NKC / group_chunks<NKC>();  // K groups per tile
-      float acc[kHalf];
-      if constexpr (GPT > 1) {
-        ok = drain_group<NB, true>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
-#pragma unroll 1
-        for (int grp = 1; grp < GPT - 1 && ok; ++grp)
-          ok = drain_group<NB, false>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
-      } else {
 #pragma unroll
-        for (int e = 0; e < kHalf; ++e) acc[e] = 0.0f;
-      }
-      // The last K group is drained straight into gamma = 2^(l2 - ln2) (fp32, in acc).
-      if (ok) {
-        const uint32_t buf = gcount % NB, use = gcount / NB;
-        ok = __all_sync(0xffffffffu, mbar_wait(TFULL0 + 8u * buf, use & 1u, kErrWaitTmemFull));
-        if (ok) {
-          tc_fence_after();
-#pragma unroll
-          for (int hh = 0; hh < kHalf / 16; ++hh) {
-            float v[16];
-            tmem_ld16(lane_tmem + buf * NC + hh * 16, v);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const int col = hh * 16 + e;
-              const float l2 = fmaf(acc[col] + v[e], -0.5f * kLog2e, cp[col]);
-              acc[col] = valid ? ex2(l2 - ln2) : 0.0f;
-            }
-          }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(TEMPTY0 + 8u * buf);
-          ++gcount;
-        }
-      }
-      // the previous tile's statistics leave TMEM before this tile's round 0 starts
-      if (ok && i > 0)
-        ok = drain_stats<NKC, NSR == 2>(i - 1, SFULL, SEMPTY, lane_q + kColStats,
-                                        lane_q + kColStats1, half, lane, k < K ? dst : nullptr);
-      ok = epi_sync_and(ok);
-      if (!ok) break;
-      // Two rounds of 64 points: the round's rows store gamma_hi = tf32(gamma) and
-      // gamma_lo = tf32(gamma - gamma_hi) as MN-major SWIZZLE_128B_BASE32B operands
-      // gamma^T (M = component, K = point): point p' owns the 128-byte row p' of each
-      // 32-component atom (atoms 8 KB apart); its four 32-byte chunks (8 components each)
-      // sit at chunk index (c8 ^ (p' % 4)).  The two 16-byte halves of a chunk are stored
-      // in an order that differs between rows p' and p'+4, so a warp's stores hit every
-      // bank once per 128 bytes.  n_k adds gamma_hi + gamma_lo of the round's points.
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const uint32_t rc = 2u * i + r;
-        ok = __all_sync(0xffffffffu, mbar_wait(GEMPTY, (rc & 1u) ^ 1u, kErrWaitGammaEmpty));
-        if (ok && (row >> 6) == r) {
-          const int rp = row & (kRoundPts - 1);
-          uint8_t *grow = gamma + rp * 128;
-          const int flip = (rp >> 2) & 1;
-#pragma unroll
-          for (int jj = 0; jj < kHalf / 32; ++jj) {
-#pragma unroll
-            for (int c8 = 0; c8 < 4; ++c8) {
-              float gh[8], gl[8];
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const float g = acc[jj * 32 + c8 * 8 + e];
-                gh[e] = to_tf32(g);
-                gl[e] = to_tf32(g - gh[e]);
-              }
-              uint8_t *chunk = grow + (half * 2 + jj) * kGAtom + ((c8 ^ (rp & 3)) << 5);
-              const int o0 = flip << 4, o1 = (flip ^ 1) << 4;
-              *reinterpret_cast<float4 *>(chunk + o0) =
-                  flip ? make_float4(gh[4], gh[5], gh[6], gh[7]) : make_float4(gh[0], gh[1], gh[2], gh[3]);
-              *reinterpret_cast<float4 *>(chunk + o1) =
-                  flip ? make_float4(gh[0], gh[1], gh[2], gh[3]) : make_float4(gh[4], gh[5], gh[6], gh[7]);
-              *reinterpret_cast<float4 *>(chunk + kGHalf + o0) =
-                  flip ? make_float4(gl[4], gl[5], gl[6], gl[7]) : make_float4(gl[0], gl[1], gl[2], gl[3]);
-              *reinterpret_cast<float4 *>(chunk + kGHalf + o1) =
-                  flip ? make_float4(gl[0], gl[1], gl[2], gl[3]) : make_float4(gl[4], gl[5], gl[6], gl[7]);
-            }
-          }
-          // the exactly re-evaluated leading components replace their tensor-core values
-          const int cb = ct * NC + half * kHalf;
-          const int tix[2] = {ti.x, ti.y};
-          const float tlv[2] = {tl.x, tl.y};
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const int lc_ = tix[c] - cb;
-            if (valid && lc_ >= 0 && lc_ < kHalf) {
-              const float g = ex2(tlv[c] - ln2);
-              const float gh = to_tf32(g), gl = to_tf32(g - gh);
-              uint8_t *e = grow + (half * 2 + (lc_ >> 5)) * kGAtom +
-                           ((((lc_ & 31) >> 3) ^ (rp & 3)) << 5) + (lc_ & 7) * 4;
-              *reinterpret_cast<float *>(e) = gh;
-              *reinterpret_cast<float *>(e + kGHalf) = gl;
-            }
-          }
-          fence_proxy_async_smem();
-        }
-        ok = epi_sync_and(ok);  // every row of the round is in place
-        if (!ok) break;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(GFULL);
-        {
-          const uint8_t *gcol = gamma + (row >> 5) * kGAtom + (row & 7) * 4;
-          const int c8 = (row & 31) >> 3;
-          float a = 0.0f;
-#pragma unroll 8
-          for (int pp = half * 32; pp < half * 32 + 32; ++pp) {
-            const int off = pp * 128 + ((c8 ^ (pp & 3)) << 5);
-            a += *reinterpret_cast<const float *>(gcol + off) +
-                 *reinterpret_cast<const float *>(gcol + kGHalf + off);
-          }
-          nk += a;
-        }
-        ok = epi_sync_and(ok);  // gamma reads done before the next round's writes
-        if (!ok) break;
-      }
-      if (!ok) break;
+    for (int e = 0; e < SEG; e += 4) {
+      const int f = seg * SEG + e;  // feature column: x^2 part first, then x
+      float *o = dst + (f < DP ? DP + f : f - DP);
+      *reinterpret_cast<float4 *>(o) = ok ? make_float4(sacc[e], sacc[e + 1], sacc[e + 2], sacc[e + 3])
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    if (ok && T > 0)
-      ok = drain_stats<NKC, NSR == 2>(T - 1, SFULL, SEMPTY, lane_q + kColStats,
-                                      lane_q + kColStats1, half, lane, k < K ? dst : nullptr);
-    ok = epi_sync_and(ok);
-    if (half == 1) nk_x[row] = nk;
-    epi_sync_and(true);
-    if (k < K) {
-      if (!ok || T == 0) {
-        for (int f = half * DP; f < (half + 1) * DP; ++f) dst[f] = 0.0f;
-      }
-      if (half == 0) dst[2 * DP] = (ok && T > 0) ? nk + nk_x[row] : 0.0f;
-    }
+  }
+  // n_k: the 32 threads that share a component chunk add their sums in a fixed order
+  // (every MMA is complete, so round buffer 0 is free)
+  float *nk_s = reinterpret_cast<float *>(smem);  // [32 points][128 components]
+#pragma unroll
+  for (int e = 0; e < 8; ++e) nk_s[pr * NC + cg * 8 + e] = nk[e];
+  __syncthreads();
+  if (wt < NC) {
+    float a = 0.0f;
+    for (int p = 0; p < kRoundPts2; ++p) a += nk_s[p * NC + wt];
+    const int kk = ct * NC + wt;
+    if (kk < K) partial[((int64_t)slot * K + kk) * PSTRIDE + 2 * DP] = ok ? a : 0.0f;
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -975,13 +849,13 @@ TcPlan plan(int64_t N, int d, int K) {
   p.tpg = (int)cdiv(p.n_ct, G);
   p.G = (int)cdiv(p.n_ct, p.tpg);
   p.grid1 = (int)std::min<int64_t>((int64_t)p.n_pt * p.G, sms);
-  p.S = std::max(1, std::min(sms / std::max(1, p.n_ct), p.n_pt));
+  p.S = (int)std::max<int64_t>(1, std::min<int64_t>(sms / std::max(1, p.n_ct), cdiv(N, 32)));
   p.grid2 = p.n_ct * p.S;
   return p;
 }
 
 struct TcWs {
-  float *qhi, *qlo, *cst2, *sc, *ms, *lc, *part_m, *part_s, *ln2x, *partial;
+  float *qhi, *qlo, *cst2, *sc, *ms, *lc, *part_m, *part_s, *ln2x, *partial, *L;
   float2 *part_tv, *top_l;
   int2 *part_ti, *top_i;
   double *ln_part;
@@ -1009,12 +883,13 @@ TcWs tc_layout(void *ws, const TcPlan &p) {
   w.top_i = c.take<int2>(p.N);
   w.partial = c.take<float>((size_t)p.S * p.K * (2 * p.dp + 4));
   w.ln_part = c.take<double>(kRefineBlocks);
+  w.L = c.take<float>((size_t)p.N * p.Kp);
   w.bytes = c.bytes();
   return w;
 }
 
 size_t smem1_bytes() { return 1024 + kStages1 * kStageBytes + 256 + 128 * 24; }
-size_t smem2_bytes() { return 1024 + kStages2 * kStageBytes + kGammaBytes + 1024; }
+size_t smem2_bytes() { return 1024 + 2 * kBuf2 + 128; }
 
 template <int NKC>
 int tc_launch(const TcPlan &p, const float *X, const float *pts, const TcWs &w, float *ln,
@@ -1022,25 +897,23 @@ int tc_launch(const TcPlan &p, const float *X, const float *pts, const TcWs &w, 
   const float *phi = pts;
   const float *plo = pts + points_half_floats(p.N, p.d);
   const int64_t rows = npad_of(p.N);
-  CUtensorMap m_phi, m_plo, m_phi32, m_plo32, m_qhi, m_qlo;
+  CUtensorMap m_phi, m_plo, m_qhi, m_qlo;
   int rc;
   if ((rc = make_map(&m_phi, phi, rows, p.KA, BM))) return rc;
   if ((rc = make_map(&m_plo, plo, rows, p.KA, BM))) return rc;
-  if ((rc = make_map(&m_phi32, phi, rows, p.KA, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))) return rc;
-  if ((rc = make_map(&m_plo32, plo, rows, p.KA, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))) return rc;
   if ((rc = make_map(&m_qhi, w.qhi, p.Kp, p.KA, NC))) return rc;
   if ((rc = make_map(&m_qlo, w.qlo, p.Kp, p.KA, NC))) return rc;
   static bool attr_done[5] = {};
   if (!attr_done[NKC / 2]) {
     FGMM_CUDA_TRY(cudaFuncSetAttribute(tc_pass1_kernel<NKC>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1_bytes()));
-    FGMM_CUDA_TRY(cudaFuncSetAttribute(tc_pass2_kernel<NKC>,
+    FGMM_CUDA_TRY(cudaFuncSetAttribute(tc_stats_kernel<NKC>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2_bytes()));
     attr_done[NKC / 2] = true;
   }
   tc_pass1_kernel<NKC><<<p.grid1, kThreads, smem1_bytes(), st>>>(
       m_phi, m_plo, m_qhi, m_qlo, w.cst2, p.N, p.n_pt, p.n_ct, p.G, p.tpg, w.part_m, w.part_s,
-      w.part_tv, w.part_ti);
+      w.part_tv, w.part_ti, w.L, p.Kp);
   FGMM_LAUNCH_CHECK("tc_pass1_kernel");
   mark(st, "tc_pass1_kernel");
   {
@@ -1060,11 +933,11 @@ int tc_launch(const TcPlan &p, const float *X, const float *pts, const TcWs &w, 
     FGMM_LAUNCH_CHECK("tc_refine_kernel");
     mark(st, "tc_refine_kernel");
   }
-  tc_pass2_kernel<NKC><<<p.grid2, kThreads, smem2_bytes(), st>>>(
-      m_phi, m_plo, m_phi32, m_plo32, m_qhi, m_qlo, w.cst2, w.ln2x, w.top_i, w.top_l, p.N,
-      p.n_pt, p.S, p.K, w.partial);
-  FGMM_LAUNCH_CHECK("tc_pass2_kernel");
-  mark(st, "tc_pass2_kernel");
+  const int x_vec = (p.d % 4 == 0) && (reinterpret_cast<uintptr_t>(X) % 16 == 0);
+  tc_stats_kernel<NKC><<<p.grid2, kThreads2, smem2_bytes(), st>>>(
+      X, p.d, x_vec, w.L, p.Kp, w.ln2x, w.top_i, w.top_l, p.N, p.S, p.K, w.partial);
+  FGMM_LAUNCH_CHECK("tc_stats_kernel");
+  mark(st, "tc_stats_kernel");
   return FGMM_OK;
 }
 
