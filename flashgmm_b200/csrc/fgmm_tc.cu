@@ -427,7 +427,8 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
 // the direct form of flash_gmm/csrc/flash_gmm_cpu.cpp:30-45 (fp32, with
 // w = x var^{-1/2} - mu var^{-1/2} formed by one FMA), swaps them into the log-sum-exp,
 // and writes the log-normalizer (output and log2 form for pass 2), the two exact
-// log2-likelihoods with their component indices, and one log-normalizer sum per block.
+// log2-likelihoods over their tensor-core values in L, and one log-normalizer sum per
+// block.
 // Eight lanes per point (four points per warp), lanes striped over the dimensions; all
 // loads of a point are issued before its reductions.
 template <int DPL>  // dimensions per lane: ceil(d / 8)
@@ -436,7 +437,7 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
                  const float *__restrict__ ms, const float *__restrict__ lc,
                  const float *__restrict__ part_m, const float *__restrict__ part_s,
                  const float2 *__restrict__ part_tv, const int2 *__restrict__ part_ti, int G,
-                 float *__restrict__ ln2x, int2 *__restrict__ top_i, float2 *__restrict__ top_l,
+                 float *__restrict__ ln2x, float *__restrict__ L, int Kp,
                  float *__restrict__ ln_out, double *__restrict__ ln_part) {
   __shared__ double wsum[8];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -508,8 +509,8 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
     const float ln2 = m + __log2f(tot);
     if (live && sub == 0) {
       ln2x[n] = ln2;
-      top_i[n] = make_int2(j1, j2);
-      top_l[n] = make_float2(e1, e2);
+      if (j1 >= 0) L[n * Kp + j1] = e1;
+      if (j2 >= 0) L[n * Kp + j2] = e2;
       const float l = ln2 * kLn2;
       ln_out[n] = l;
       acc += (double)l;
@@ -528,94 +529,90 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
 
 // ------------------------------------------------------------------------- pass 2
 // Statistics GEMM S[k, f] = sum_n gamma[n, k] F[n, f] with F = [x^2 | x] (3xTF32), the
-// only tensor-core work left once pass 1 has stored the log2-likelihood matrix L.
-// A CTA owns 128 components (the M of the MMA) and a contiguous range of points, taken
-// in rounds of 32 points (the K of four MMA k-steps).  Its sixteen warps build each
-// round's operands straight from global memory: gamma = 2^(L - ln2) with the two
-// refined components replaced by their exact values, and F from X, both split into
-// tf32 hi/lo in the MN-major SWIZZLE_128B_BASE32B layout, double-buffered; after a
-// barrier one thread issues the round's MMAs.  The accumulator alternates between two
-// TMEM regions every kRoundsFlush rounds; while the tensor pipe fills one region the
-// warps add the other into fp32 registers, so tensor-memory accumulation (not
-// round-to-nearest) never spans more than 128 points and the running sums stay on chip
-// until the CTA ends.
-constexpr int kRoundPts2 = 32;
-constexpr int kRoundsFlush = 4;
-constexpr int kWorkWarps = 16;
-constexpr int kThreads2 = 32 * kWorkWarps;
-constexpr int kAtom2 = kRoundPts2 * 128;         // 4 KB: 32 points x 32 fp32
-constexpr int kGOff2 = 0, kGLoOff2 = 4 * kAtom2;  // gamma^T hi / lo: 4 component atoms each
-constexpr int kFOff2 = 8 * kAtom2;                // F hi: up to 8 feature atoms
-constexpr int kFLoOff2 = kFOff2 + 8 * kAtom2;     // F lo
-constexpr int kBuf2 = kFLoOff2 + 8 * kAtom2;      // 96 KB per round buffer
+// only tensor-core work left once pass 1 has stored the log2-likelihood matrix L (with
+// the refined leading components written over their tensor-core values).  A CTA owns
+// 128 components (the M of the MMA, on the TMEM lanes) and a contiguous range of points,
+// taken in slices of 16 points (the K of two MMA k-steps).  Warp roles (16 warps):
+//   warp 5 lane 0 (producer): per slice, TMA of F hi and F lo from the prepared points
+//     buffer (one 3-D box each: 16 points x all 32-feature atoms, MN-major
+//     SWIZZLE_128B_ATOM_32B), of the slice's L tile [16 points][128 components] and of
+//     its 16 log2-normalizers, into a ring of kStages slices;
+//   warps 0-3 (gamma): warp q computes gamma = 2^(L - ln2) for components 32q..32q+31
+//     (its TMEM lane quarter) at the slice's 16 points, splits it into tf32 hi / lo and
+//     stores both to a TMEM gamma buffer (ring of kGBufs), the MMA's A operand;
+//   warp 4 lane 0 (MMA): six MMAs per slice (gamma_lo F_hi, gamma_hi F_lo, then
+//     gamma_hi F_hi, two k-steps each) into the statistics accumulator;
+//   all 16 warps: every kSlicesFlush slices (128 points) the accumulator is added into
+//     fp32 registers (warp w: lane quarter w % 4, a quarter of the columns), because
+//     tensor-memory accumulation does not round to nearest.  With two accumulator
+//     regions (KA <= 192) the tensor pipe fills one while the other drains; at KA = 256
+//     the single region is drained between tiles.
+// Every hand-off is an mbarrier; no barrier spans the CTA inside the loop.
+constexpr int kSlicePts = 16;
+constexpr int kSlicesFlush = 8;
+constexpr int kGBufs = 4;
+constexpr int kThreads2 = 512;
+constexpr int kGCols = 2 * kSlicePts;  // TMEM columns of one gamma buffer (hi | lo)
+
+template <int KA>
+struct StatsShape {
+  static constexpr int kAtom = kSlicePts * 128;                // 2 KB: 16 points x 32 fp32
+  static constexpr int kFPart = (KA / 32) * kAtom;             // F hi (or lo) of a slice
+  static constexpr int kLOff = 2 * kFPart;                     // L tile [16][128]
+  static constexpr int kNOff = kLOff + kSlicePts * NC * 4;     // ln2 [16]
+  static constexpr int kStage = (kNOff + kSlicePts * 4 + 1023) / 1024 * 1024;
+  static constexpr int kStagesFit = (220 * 1024) / kStage;
+  static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
+  static constexpr int kSmem = 1024 + kStages * kStage + 512;
+};
 
 __device__ __forceinline__ bool cta_sync_and(bool v) {
   return __syncthreads_and(v ? 1 : 0) != 0;
 }
 
-// Stores 8 consecutive fp32 (one 32-byte chunk of a 128-byte MN-major row) as hi and lo
-// tf32 parts.  The two 16-byte halves are stored in an order that alternates between odd
-// and even atoms, so a warp's stores (16 chunks of 2 rows over 4 atoms) hit every bank once
-// per 128 bytes.
-__device__ __forceinline__ void put_chunk8(uint8_t *hi, uint8_t *lo, const float (&v)[8], int flip) {
-  float h[8], l[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    h[e] = to_tf32(v[e]);
-    l[e] = to_tf32(v[e] - h[e]);
-  }
-  const float4 h0 = make_float4(h[0], h[1], h[2], h[3]), h1 = make_float4(h[4], h[5], h[6], h[7]);
-  const float4 l0 = make_float4(l[0], l[1], l[2], l[3]), l1 = make_float4(l[4], l[5], l[6], l[7]);
-  const int o0 = flip << 4, o1 = (flip ^ 1) << 4;  // store order only; data stays in place
-  *reinterpret_cast<float4 *>(hi + o0) = flip ? h1 : h0;
-  *reinterpret_cast<float4 *>(hi + o1) = flip ? h0 : h1;
-  *reinterpret_cast<float4 *>(lo + o0) = flip ? l1 : l0;
-  *reinterpret_cast<float4 *>(lo + o1) = flip ? l0 : l1;
-}
-
-// Inputs one thread needs for one round (prefetched a round ahead).
-struct RoundIn {
-  float l[8];   // log2-likelihoods of the thread's 8 components at its point
-  float x[8];   // 8 coordinates of the thread's feature chunk
-  float ln2;    // the point's log2-normalizer
-  int2 ti;      // its two refined components
-  float2 tl;    // and their exact log2-likelihoods
-};
-
 // Partial statistics row (per CTA slot and component): [s (DP) | sq (DP) | n | pad],
 // stride 2 DP + 4.
 template <int NKC>
 __global__ void __launch_bounds__(kThreads2, 1)
-tc_stats_kernel(const float *__restrict__ X, int d, int x_vec, const float *__restrict__ L,
-                int Kp, const float *__restrict__ ln2x, const int2 *__restrict__ top_i,
-                const float2 *__restrict__ top_l, int64_t N, int S_slots, int K,
-                float *__restrict__ partial) {
+tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constant__ CUtensorMap tm_flo,
+                const __grid_constant__ CUtensorMap tm_l, const float *__restrict__ ln2x, int64_t N,
+                int S_slots, int K, float *__restrict__ partial) {
   constexpr int KA = NKC * KC;
   constexpr int DP = KA / 2;
   constexpr int PSTRIDE = 2 * DP + 4;
-  constexpr int SEG = KA / 4;  // statistics columns per thread
-  constexpr int FCH = DP / 8;  // 8-feature chunks per point
-  static_assert(2 * KA <= 512, "two statistics regions must fit in TMEM");
+  constexpr int SEG = KA / 4;  // statistics columns per warp
+  constexpr int NSR = 2 * KA + kGBufs * kGCols <= 512 ? 2 : 1;  // accumulator regions
+  constexpr uint32_t kGBase = NSR * KA;                           // TMEM column of gamma buffer 0
+  using Sh = StatsShape<KA>;
+  constexpr int NST = Sh::kStages;
+  static_assert(NSR * KA + kGBufs * kGCols <= 512, "TMEM budget");
   static_assert(SEG % 16 == 0, "statistics segment of whole 16-column loads");
+  static_assert(NST >= 2, "shared-memory budget");
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = align1024(smem_raw);
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 2 * kBuf2);
-  // bars: gempty[2] sfull[2] done
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 5);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + NST * Sh::kStage);
+  // bars: full[NST] empty[NST] gfull[G] gempty[G] sfull[2] sempty[2] done
   const uint32_t bar0 = smem_u32(bars);
-  auto GEMPTY = [&](int b) { return bar0 + 8u * b; };
-  auto SFULL = [&](int b) { return bar0 + 8u * (2 + b); };
-  const uint32_t DONE = bar0 + 8u * 4;
+  auto FULL = [&](int s) { return bar0 + 8u * s; };
+  auto EMPTY = [&](int s) { return bar0 + 8u * (NST + s); };
+  auto GFULL = [&](int g) { return bar0 + 8u * (2 * NST + g); };
+  auto GEMPTY = [&](int g) { return bar0 + 8u * (2 * NST + kGBufs + g); };
+  auto SFULL = [&](int r) { return bar0 + 8u * (2 * NST + 2 * kGBufs + r); };
+  auto SEMPTY = [&](int r) { return bar0 + 8u * (2 * NST + 2 * kGBufs + 2 + r); };
+  const uint32_t DONE = bar0 + 8u * (2 * NST + 2 * kGBufs + 4);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * NST + 2 * kGBufs + 5);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int wt = threadIdx.x;
   const int ct = blockIdx.x / S_slots, slot = blockIdx.x % S_slots;
-  const int64_t n_rounds = (N + kRoundPts2 - 1) / kRoundPts2;
-  const int64_t r0 = slot * n_rounds / S_slots, r1 = (slot + 1) * n_rounds / S_slots;
-  const int R = (int)(r1 - r0);
+  const int64_t n_sl = (N + kSlicePts - 1) / kSlicePts;
+  const int64_t s0 = slot * n_sl / S_slots, s1 = (slot + 1) * n_sl / S_slots;
+  const int S = (int)(s1 - s0);                        // slices of this CTA
+  const int T = (S + kSlicesFlush - 1) / kSlicesFlush;  // flush tiles
 
   if (threadIdx.x == 0) {
-    for (int b = 0; b < 2; ++b) { mbar_init(GEMPTY(b), 1); mbar_init(SFULL(b), 1); }
+    for (int i = 0; i < NST; ++i) { mbar_init(FULL(i), 1); mbar_init(EMPTY(i), 1 + 4); }
+    for (int g = 0; g < kGBufs; ++g) { mbar_init(GFULL(g), 4); mbar_init(GEMPTY(g), 1); }
+    for (int r = 0; r < 2; ++r) { mbar_init(SFULL(r), 1); mbar_init(SEMPTY(r), 16); }
     mbar_init(DONE, 1);
     fence_mbar_init();
   }
@@ -629,147 +626,149 @@ tc_stats_kernel(const float *__restrict__ X, int d, int x_vec, const float *__re
   const uint32_t tmem = *tmem_slot;
 
   const int q = warp & 3, seg = warp >> 2;  // TMEM lane quarter, column segment
-  const uint32_t lane_tmem = tmem + ((uint32_t)(q * 32) << 16) + seg * SEG;
-  // gamma role: point pr of the round, components cg*8 .. cg*8+7 of this CTA's 128
-  const int pr = wt >> 4, cg = wt & 15;
-  const int ga = cg >> 2, gc8 = cg & 3;
-  const int kb = ct * NC + cg * 8;
-  // feature role: point fp, feature chunk fc (the first 32 * FCH threads)
-  const bool f_on = wt < kRoundPts2 * FCH;
-  const int fp = wt / FCH, fc = wt % FCH;
-  const int fa = fc >> 2, fc8 = fc & 3;
+  const uint32_t lane_tmem = tmem + ((uint32_t)(q * 32) << 16);
+  const int cl = q * 32 + lane;             // component of this lane within the CTA's 128
   float sacc[SEG];
 #pragma unroll
   for (int e = 0; e < SEG; ++e) sacc[e] = 0.0f;
-  float nk[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) nk[e] = 0.0f;
+  int nf = 0;  // next tile this warp drains
+  bool ok = true;
 
-  auto fetch = [&](int r, RoundIn &in) {
-    const int64_t nb = (r0 + r) * kRoundPts2;
-    const int64_t n = nb + pr;
-    if (n < N) {
-      const float4 *lp = reinterpret_cast<const float4 *>(L + n * Kp + kb);
-      const float4 a = __ldg(lp), c = __ldg(lp + 1);
-      in.l[0] = a.x; in.l[1] = a.y; in.l[2] = a.z; in.l[3] = a.w;
-      in.l[4] = c.x; in.l[5] = c.y; in.l[6] = c.z; in.l[7] = c.w;
-      in.ln2 = __ldg(ln2x + n);
-      in.ti = top_i[n];
-      in.tl = top_l[n];
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) in.l[e] = -INFINITY;
-      in.ln2 = 0.0f;
-      in.ti = make_int2(-1, -1);
-      in.tl = make_float2(0.0f, 0.0f);
-    }
-    const int64_t m = nb + fp;
-    const int j0 = fc * 8;
-    if (f_on && m < N && x_vec && j0 + 8 <= d) {
-      const float4 *xp = reinterpret_cast<const float4 *>(X + m * d + j0);
-      const float4 a = __ldg(xp), c = __ldg(xp + 1);
-      in.x[0] = a.x; in.x[1] = a.y; in.x[2] = a.z; in.x[3] = a.w;
-      in.x[4] = c.x; in.x[5] = c.y; in.x[6] = c.z; in.x[7] = c.w;
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        in.x[e] = (f_on && m < N && j0 + e < d) ? __ldg(X + m * d + j0 + e) : 0.0f;
-    }
-  };
-  // Adds TMEM region j & 1 (flush tile j) into sacc.
-  auto flush = [&](int j) -> bool {
-    const int sb = j & 1;
-    if (!__all_sync(0xffffffffu, mbar_wait(SFULL(sb), (j >> 1) & 1, kErrWaitStatsDone)))
-      return false;
+  // Adds accumulator region of tile nf into sacc (whole warp).
+  auto flush_next = [&]() {
+    const int j = nf++;
+    const int reg = NSR == 2 ? (j & 1) : 0;
+    ok = ok && __all_sync(0xffffffffu, mbar_wait(SFULL(reg), (j / NSR) & 1, kErrWaitStatsDone));
+    if (!ok) return;
     tc_fence_after();
 #pragma unroll
     for (int c = 0; c < SEG / 16; ++c) {
       float v[16];
-      tmem_ld16(lane_tmem + sb * KA + c * 16, v);
+      tmem_ld16(lane_tmem + reg * KA + seg * SEG + c * 16, v);
       tmem_wait_ld();
 #pragma unroll
       for (int e = 0; e < 16; ++e) sacc[c * 16 + e] += v[e];
     }
     tc_fence_before();
-    return true;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(SEMPTY(reg));
   };
 
-  bool ok = true;
-  RoundIn nxt;
-  if (R > 0) fetch(0, nxt);
-  for (int r = 0; r < R; ++r) {
-    const RoundIn cur = nxt;
-    if (r + 1 < R) fetch(r + 1, nxt);
-    const int b = r & 1;
-    // buffer b is free once the MMAs of round r - 2 have read it
-    ok = __all_sync(0xffffffffu, mbar_wait(GEMPTY(b), ((r >> 1) & 1) ^ 1, kErrWaitGammaEmpty));
-    if (ok) {
-      uint8_t *buf = smem + b * kBuf2;
-      float g[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        float l2 = cur.l[e];
-        if (kb + e == cur.ti.x) l2 = cur.tl.x;
-        if (kb + e == cur.ti.y) l2 = cur.tl.y;
-        g[e] = ex2(l2 - cur.ln2);
-        nk[e] += g[e];
-      }
-      uint8_t *grow = buf + ga * kAtom2 + pr * 128 + ((gc8 ^ (pr & 3)) << 5);
-      put_chunk8(grow + kGOff2, grow + kGLoOff2, g, ga & 1);
-      if (f_on) {
-        float x2[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) x2[e] = cur.x[e] * cur.x[e];
-        uint8_t *frow = buf + fa * kAtom2 + fp * 128 + ((fc8 ^ (fp & 3)) << 5);
-        put_chunk8(frow + kFOff2, frow + kFLoOff2, x2, fa & 1);
-        frow += (DP / 32) * kAtom2;
-        put_chunk8(frow + kFOff2, frow + kFLoOff2, cur.x, fa & 1);
-      }
-      fence_proxy_async_smem();
-    }
-    // every operand of the round is in place, and every flush issued so far is done
-    ok = cta_sync_and(ok);
-    if (!ok) break;
-    const int j = r / kRoundsFlush, sb = j & 1;
-    if (wt == 0) {
-      constexpr uint32_t idesc = idesc_tf32(NC, KA, 1, 1);  // both operands MN-major
+  float nk = 0.0f;
+  if (warp < 4) {
+    // ---------------- gamma warps
+    for (int s = 0; s < S && ok; ++s) {
+      // tile j is drained before this warp could need the MMA to have started tile j + NSR
+      while (nf < T && s >= kSlicesFlush * (nf + NSR) + kGBufs && ok) flush_next();
+      const int st = s % NST, gb = s % kGBufs;
+      ok = ok && __all_sync(0xffffffffu, mbar_wait(FULL(st), (s / NST) & 1, kErrWaitFull) &&
+                                             mbar_wait(GEMPTY(gb), ((s / kGBufs) & 1) ^ 1, kErrWaitGammaEmpty));
+      if (!ok) break;
       tc_fence_after();
-      const uint32_t base = smem_u32(smem + b * kBuf2);
-      const uint32_t dst = tmem + sb * KA;
-      const bool tile_first = r % kRoundsFlush == 0;
-      // small products (gamma_lo F_hi, gamma_hi F_lo) before gamma_hi F_hi
+      const uint8_t *stg = smem + st * Sh::kStage;
+      const float *Ls = reinterpret_cast<const float *>(stg + Sh::kLOff);
+      const float4 *ln4 = reinterpret_cast<const float4 *>(stg + Sh::kNOff);
+      const int64_t nb = (s0 + s) * kSlicePts;
+      const int live = N - nb < kSlicePts ? (int)(N - nb) : kSlicePts;
+      float gh[16], gl[16];
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const uint64_t gh = sdesc(base + kGOff2 + kk * 1024, kAtom2, 512, kSw128Base32);
-        const uint64_t gl = sdesc(base + kGLoOff2 + kk * 1024, kAtom2, 512, kSw128Base32);
-        const uint64_t fh = sdesc(base + kFOff2 + kk * 1024, kAtom2, 512, kSw128Base32);
-        const uint64_t fl = sdesc(base + kFLoOff2 + kk * 1024, kAtom2, 512, kSw128Base32);
-        mma_tf32(dst, gl, fh, idesc, (tile_first && kk == 0) ? 0u : 1u);
-        mma_tf32(dst, gh, fl, idesc, 1u);
-      }
+      for (int c = 0; c < 4; ++c) {
+        const float4 l4 = ln4[c];
+        const float ln2[4] = {l4.x, l4.y, l4.z, l4.w};
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const uint64_t gh = sdesc(base + kGOff2 + kk * 1024, kAtom2, 512, kSw128Base32);
-        const uint64_t fh = sdesc(base + kFOff2 + kk * 1024, kAtom2, 512, kSw128Base32);
-        mma_tf32(dst, gh, fh, idesc, 1u);
+        for (int e = 0; e < 4; ++e) {
+          const int p = c * 4 + e;
+          const float g = p < live ? ex2(Ls[p * NC + cl] - ln2[e]) : 0.0f;
+          nk += g;
+          gh[p] = to_tf32(g);
+          gl[p] = to_tf32(g - gh[p]);
+        }
       }
-      mma_commit(GEMPTY(b));
-      if (r % kRoundsFlush == kRoundsFlush - 1 || r == R - 1) mma_commit(SFULL(sb));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(EMPTY(st));  // this warp is done with the slice's L
+      const uint32_t ga = lane_tmem + kGBase + gb * kGCols;
+      tmem_st16(ga, gh);
+      tmem_st16(ga + kSlicePts, gl);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(GFULL(gb));
+    }
+  } else if (warp == 4) {
+    // ---------------- MMA warp
+    constexpr uint32_t idesc = idesc_tf32(NC, KA, 0, 1);  // A from TMEM, B MN-major
+    for (int s = 0; s < S && ok; ++s) {
+      const int j = s / kSlicesFlush, reg = NSR == 2 ? (j & 1) : 0;
+      const bool tile_first = s % kSlicesFlush == 0;
+      if (tile_first && j >= NSR) {
+        while (nf <= j - NSR && ok) flush_next();
+        ok = ok && __all_sync(0xffffffffu, mbar_wait(SEMPTY(reg), ((j / NSR) & 1) ^ 1, kErrWaitStatsDone));
+      }
+      const int st = s % NST, gb = s % kGBufs;
+      ok = ok && __all_sync(0xffffffffu, mbar_wait(FULL(st), (s / NST) & 1, kErrWaitFull) &&
+                                             mbar_wait(GFULL(gb), (s / kGBufs) & 1, kErrWaitGammaFull));
+      if (!ok) break;
+      if (lane == 0) {
+        tc_fence_after();
+        const uint32_t gbuf = tmem + kGBase + gb * kGCols;
+        const uint32_t dst = tmem + reg * KA;
+        const uint32_t base = smem_u32(smem + st * Sh::kStage);
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+          const uint64_t fh = sdesc(base + kk * 1024, Sh::kAtom, 512, kSw128Base32);
+          const uint64_t fl = sdesc(base + Sh::kFPart + kk * 1024, Sh::kAtom, 512, kSw128Base32);
+          mma_tf32_ta(dst, gbuf + kSlicePts + kk * 8, fh, idesc, (tile_first && kk == 0) ? 0u : 1u);
+          mma_tf32_ta(dst, gbuf + kk * 8, fl, idesc, 1u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+          const uint64_t fh = sdesc(base + kk * 1024, Sh::kAtom, 512, kSw128Base32);
+          mma_tf32_ta(dst, gbuf + kk * 8, fh, idesc, 1u);
+        }
+        mma_commit(EMPTY(st));
+        mma_commit(GEMPTY(gb));
+        if (s % kSlicesFlush == kSlicesFlush - 1 || s == S - 1) mma_commit(SFULL(reg));
+      }
+      __syncwarp();
+    }
+    if (lane == 0 && S > 0) {  // every MMA of this CTA has completed before the teardown
+      mma_commit(DONE);
+      mbar_wait_drain(DONE, 0);
     }
     __syncwarp();
-    // The previous tile's region is added into registers once this tile's first round
-    // is queued; the barrier of the next round orders it before that region's reuse
-    // (two tiles later, kRoundsFlush >= 2 rounds on).
-    if (r % kRoundsFlush == 0 && r > 0) ok = flush(j - 1);
+  } else if (warp == 5) {
+    // ---------------- producer warp
+    if (lane == 0) {
+      prefetch_tmap(&tm_fhi);
+      prefetch_tmap(&tm_flo);
+      prefetch_tmap(&tm_l);
+    }
+    for (int s = 0; s < S && ok; ++s) {
+      while (nf < T && s >= kSlicesFlush * (nf + NSR) + NST && ok) flush_next();
+      const int st = s % NST;
+      if (s >= NST) ok = ok && __all_sync(0xffffffffu, mbar_wait(EMPTY(st), ((s / NST) & 1) ^ 1, kErrWaitEmpty));
+      if (!ok) break;
+      if (lane == 0) {
+        const uint32_t base = smem_u32(smem + st * Sh::kStage);
+        const int64_t nb = (s0 + s) * kSlicePts;
+        mbar_arrive_expect_tx(FULL(st), 2 * Sh::kFPart + kSlicePts * NC * 4 + kSlicePts * 4);
+        tma_load_3d(base, &tm_fhi, 0, (int32_t)nb, 0, FULL(st));
+        tma_load_3d(base + Sh::kFPart, &tm_flo, 0, (int32_t)nb, 0, FULL(st));
+        tma_load_2d(base + Sh::kLOff, &tm_l, ct * NC, (int32_t)nb, FULL(st));
+        bulk_load(base + Sh::kNOff, ln2x + nb, kSlicePts * 4, FULL(st));
+      }
+      __syncwarp();
+    }
+    // no copy may land after the CTA ends: the last NST slices' loads must be complete
+    if (lane == 0)
+      for (int s = (S > NST ? S - NST : 0); s < S; ++s) mbar_wait_drain(FULL(s % NST), (s / NST) & 1);
+    __syncwarp();
   }
-  if (ok && R > 0) ok = flush((R - 1) / kRoundsFlush);
-  // no MMA of this CTA may still run at the teardown (also after an early exit)
-  if (wt == 0 && R > 0) {
-    mma_commit(DONE);
-    mbar_wait(DONE, 0, kErrWaitDrain);
-  }
+  // every warp drains the tiles it has not drained yet
+  while (nf < T && ok) flush_next();
+
   ok = cta_sync_and(ok);
-  const int k = ct * NC + q * 32 + lane;  // TMEM lane = component
+  const int k = ct * NC + cl;
   if (k < K) {
     float *dst = partial + ((int64_t)slot * K + k) * PSTRIDE;
 #pragma unroll
@@ -779,18 +778,7 @@ tc_stats_kernel(const float *__restrict__ X, int d, int x_vec, const float *__re
       *reinterpret_cast<float4 *>(o) = ok ? make_float4(sacc[e], sacc[e + 1], sacc[e + 2], sacc[e + 3])
                                           : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-  }
-  // n_k: the 32 threads that share a component chunk add their sums in a fixed order
-  // (every MMA is complete, so round buffer 0 is free)
-  float *nk_s = reinterpret_cast<float *>(smem);  // [32 points][128 components]
-#pragma unroll
-  for (int e = 0; e < 8; ++e) nk_s[pr * NC + cg * 8 + e] = nk[e];
-  __syncthreads();
-  if (wt < NC) {
-    float a = 0.0f;
-    for (int p = 0; p < kRoundPts2; ++p) a += nk_s[p * NC + wt];
-    const int kk = ct * NC + wt;
-    if (kk < K) partial[((int64_t)slot * K + kk) * PSTRIDE + 2 * DP] = ok ? a : 0.0f;
+    if (warp < 4) dst[2 * DP] = ok ? nk : 0.0f;
   }
   tc_fence_before();
   __syncthreads();
@@ -814,14 +802,31 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// Row-major fp32 [rows][cols] matrix, box [box_rows][32] (128-byte rows) with the given swizzle.
+// Row-major fp32 [rows][cols] matrix, box [box_rows][box_cols] with the given swizzle.
+// Row-major fp32 [rows][cols] matrix (cols a multiple of 32) seen as 32-column atoms:
+// box = 32 rows x all atoms, landing as [atom][row][32] with SWIZZLE_128B_ATOM_32B (the
+// MN-major operand layout of the statistics GEMM).
+int make_map_atoms(CUtensorMap *m, const float *base, int64_t rows, int cols, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return fail(FGMM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {(cuuint64_t)KC, (cuuint64_t)rows, (cuuint64_t)(cols / KC)};
+  cuuint64_t strides[2] = {(cuuint64_t)cols * sizeof(float), (cuuint64_t)KC * sizeof(float)};
+  cuuint32_t box[3] = {(cuuint32_t)KC, (cuuint32_t)box_rows, (cuuint32_t)(cols / KC)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FGMM_ERR_CUDA, "cuTensorMapEncodeTiled (atoms) failed: " + std::to_string((int)r));
+  return FGMM_OK;
+}
+
 int make_map(CUtensorMap *m, const float *base, int64_t rows, int cols, int box_rows,
-             CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+             CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B, int box_cols = KC) {
   auto fn = encode_fn();
   if (!fn) return fail(FGMM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)cols * sizeof(float)};
-  cuuint32_t box[2] = {(cuuint32_t)KC, (cuuint32_t)box_rows};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
@@ -856,8 +861,8 @@ TcPlan plan(int64_t N, int d, int K) {
 
 struct TcWs {
   float *qhi, *qlo, *cst2, *sc, *ms, *lc, *part_m, *part_s, *ln2x, *partial, *L;
-  float2 *part_tv, *top_l;
-  int2 *part_ti, *top_i;
+  float2 *part_tv;
+  int2 *part_ti;
   double *ln_part;
   size_t bytes;
 };
@@ -879,8 +884,6 @@ TcWs tc_layout(void *ws, const TcPlan &p) {
   w.part_tv = c.take<float2>((size_t)p.G * p.N);
   w.part_ti = c.take<int2>((size_t)p.G * p.N);
   w.ln2x = c.take<float>(p.N);
-  w.top_l = c.take<float2>(p.N);
-  w.top_i = c.take<int2>(p.N);
   w.partial = c.take<float>((size_t)p.S * p.K * (2 * p.dp + 4));
   w.ln_part = c.take<double>(kRefineBlocks);
   w.L = c.take<float>((size_t)p.N * p.Kp);
@@ -889,8 +892,14 @@ TcWs tc_layout(void *ws, const TcPlan &p) {
 }
 
 size_t smem1_bytes() { return 1024 + kStages1 * kStageBytes + 256 + 128 * 24; }
-size_t smem2_bytes() { return 1024 + 2 * kBuf2 + 128; }
-
+size_t smem2_bytes(int KA) {
+  switch (KA) {
+    case 64: return StatsShape<64>::kSmem;
+    case 128: return StatsShape<128>::kSmem;
+    case 192: return StatsShape<192>::kSmem;
+    default: return StatsShape<256>::kSmem;
+  }
+}
 template <int NKC>
 int tc_launch(const TcPlan &p, const float *X, const float *pts, const TcWs &w, float *ln,
               cudaStream_t st) {
@@ -908,7 +917,7 @@ int tc_launch(const TcPlan &p, const float *X, const float *pts, const TcWs &w, 
     FGMM_CUDA_TRY(cudaFuncSetAttribute(tc_pass1_kernel<NKC>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1_bytes()));
     FGMM_CUDA_TRY(cudaFuncSetAttribute(tc_stats_kernel<NKC>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2_bytes()));
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2_bytes(NKC * KC)));
     attr_done[NKC / 2] = true;
   }
   tc_pass1_kernel<NKC><<<p.grid1, kThreads, smem1_bytes(), st>>>(
@@ -921,8 +930,8 @@ int tc_launch(const TcPlan &p, const float *X, const float *pts, const TcWs &w, 
     const int dpl = (p.d + 7) / 8;
 #define FGMM_REFINE(D)                                                                          \
   tc_refine_kernel<D><<<blocks, 256, 0, st>>>(X, p.N, p.d, w.sc, w.ms, w.lc, w.part_m, w.part_s, \
-                                              w.part_tv, w.part_ti, p.G, w.ln2x, w.top_i,       \
-                                              w.top_l, ln, w.ln_part)
+                                              w.part_tv, w.part_ti, p.G, w.ln2x, w.L, p.Kp,     \
+                                              ln, w.ln_part)
     if (dpl <= 1) FGMM_REFINE(1);
     else if (dpl <= 2) FGMM_REFINE(2);
     else if (dpl <= 4) FGMM_REFINE(4);
@@ -933,9 +942,12 @@ int tc_launch(const TcPlan &p, const float *X, const float *pts, const TcWs &w, 
     FGMM_LAUNCH_CHECK("tc_refine_kernel");
     mark(st, "tc_refine_kernel");
   }
-  const int x_vec = (p.d % 4 == 0) && (reinterpret_cast<uintptr_t>(X) % 16 == 0);
-  tc_stats_kernel<NKC><<<p.grid2, kThreads2, smem2_bytes(), st>>>(
-      X, p.d, x_vec, w.L, p.Kp, w.ln2x, w.top_i, w.top_l, p.N, p.S, p.K, w.partial);
+  CUtensorMap m_fhi, m_flo, m_l;
+  if ((rc = make_map_atoms(&m_fhi, phi, rows, p.KA, kSlicePts))) return rc;
+  if ((rc = make_map_atoms(&m_flo, plo, rows, p.KA, kSlicePts))) return rc;
+  if ((rc = make_map(&m_l, w.L, p.N, p.Kp, kSlicePts, CU_TENSOR_MAP_SWIZZLE_NONE, NC))) return rc;
+  tc_stats_kernel<NKC><<<p.grid2, kThreads2, smem2_bytes(NKC * KC), st>>>(
+      m_fhi, m_flo, m_l, w.ln2x, p.N, p.S, p.K, w.partial);
   FGMM_LAUNCH_CHECK("tc_stats_kernel");
   mark(st, "tc_stats_kernel");
   return FGMM_OK;
@@ -985,6 +997,12 @@ int tc_em_stats(const float *X, const void *points, int64_t N, int d, const floa
                          st);
 }
 
+#ifdef FGMM_EXP_TIMING
+extern "C" int fgmm_exp_timing(unsigned long long *out, int n) {
+  cudaDeviceSynchronize();
+  return (int)cudaMemcpyFromSymbol(out, g_tim, sizeof(unsigned long long) * 8 * n);
+}
+#endif
 int tc_device_error(bool reset) {
   int v = 0;
   if (cudaDeviceSynchronize() != cudaSuccess) return -1;
