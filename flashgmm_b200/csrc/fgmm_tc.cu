@@ -533,25 +533,28 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
 // the refined leading components written over their tensor-core values).  A CTA owns
 // 128 components (the M of the MMA, on the TMEM lanes) and a contiguous range of points,
 // taken in slices of 16 points (the K of two MMA k-steps).  Warp roles (16 warps):
-//   warp 5 lane 0 (producer): per slice, TMA of F hi and F lo from the prepared points
+//   warp 9 lane 0 (producer): per slice, TMA of F hi and F lo from the prepared points
 //     buffer (one 3-D box each: 16 points x all 32-feature atoms, MN-major
 //     SWIZZLE_128B_ATOM_32B), of the slice's L tile [16 points][128 components] and of
 //     its 16 log2-normalizers, into a ring of kStages slices;
-//   warps 0-3 (gamma): warp q computes gamma = 2^(L - ln2) for components 32q..32q+31
-//     (its TMEM lane quarter) at the slice's 16 points, splits it into tf32 hi / lo and
-//     stores both to a TMEM gamma buffer (ring of kGBufs), the MMA's A operand;
-//   warp 4 lane 0 (MMA): six MMAs per slice (gamma_lo F_hi, gamma_hi F_lo, then
+//   warps 0-7 (gamma): warp w computes gamma = 2^(L - ln2) for components
+//     32 (w % 4) .. +31 (its TMEM lane quarter) at 8 of the slice's 16 points, splits it
+//     into tf32 hi / lo and stores both to a TMEM gamma buffer (ring of kGBufs), the
+//     MMA's A operand;
+//   warp 8 lane 0 (MMA): six MMAs per slice (gamma_lo F_hi, gamma_hi F_lo, then
 //     gamma_hi F_hi, two k-steps each) into the statistics accumulator;
 //   all 16 warps: every kSlicesFlush slices (128 points) the accumulator is added into
 //     fp32 registers (warp w: lane quarter w % 4, a quarter of the columns), because
 //     tensor-memory accumulation does not round to nearest.  With two accumulator
 //     regions (KA <= 192) the tensor pipe fills one while the other drains; at KA = 256
-//     the single region is drained between tiles.
+//     the single region is drained between tiles.  Warps waiting only for a drain sleep
+//     between polls.
 // Every hand-off is an mbarrier; no barrier spans the CTA inside the loop.
 constexpr int kSlicePts = 16;
 constexpr int kSlicesFlush = 8;
 constexpr int kGBufs = 4;
 constexpr int kThreads2 = 512;
+constexpr int kGammaWarps = 8;
 constexpr int kGCols = 2 * kSlicePts;  // TMEM columns of one gamma buffer (hi | lo)
 
 template <int KA>
@@ -570,6 +573,9 @@ __device__ __forceinline__ bool cta_sync_and(bool v) {
   return __syncthreads_and(v ? 1 : 0) != 0;
 }
 
+#ifdef FGMM_EXP_TIMING
+__device__ unsigned long long g_tim[2048][8];
+#endif
 // Partial statistics row (per CTA slot and component): [s (DP) | sq (DP) | n | pad],
 // stride 2 DP + 4.
 template <int NKC>
@@ -610,8 +616,8 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
   const int T = (S + kSlicesFlush - 1) / kSlicesFlush;  // flush tiles
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < NST; ++i) { mbar_init(FULL(i), 1); mbar_init(EMPTY(i), 1 + 4); }
-    for (int g = 0; g < kGBufs; ++g) { mbar_init(GFULL(g), 4); mbar_init(GEMPTY(g), 1); }
+    for (int i = 0; i < NST; ++i) { mbar_init(FULL(i), 1); mbar_init(EMPTY(i), 1 + kGammaWarps); }
+    for (int g = 0; g < kGBufs; ++g) { mbar_init(GFULL(g), kGammaWarps); mbar_init(GEMPTY(g), 1); }
     for (int r = 0; r < 2; ++r) { mbar_init(SFULL(r), 1); mbar_init(SEMPTY(r), 16); }
     mbar_init(DONE, 1);
     fence_mbar_init();
@@ -635,10 +641,11 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
   bool ok = true;
 
   // Adds accumulator region of tile nf into sacc (whole warp).
-  auto flush_next = [&]() {
+  auto flush_next = [&](bool sleep) {
     const int j = nf++;
     const int reg = NSR == 2 ? (j & 1) : 0;
-    ok = ok && __all_sync(0xffffffffu, mbar_wait(SFULL(reg), (j / NSR) & 1, kErrWaitStatsDone));
+    ok = ok && __all_sync(0xffffffffu, sleep ? mbar_wait_sleep(SFULL(reg), (j / NSR) & 1, kErrWaitStatsDone)
+                                             : mbar_wait(SFULL(reg), (j / NSR) & 1, kErrWaitStatsDone));
     if (!ok) return;
     tc_fence_after();
 #pragma unroll
@@ -654,31 +661,49 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
     if (lane == 0) mbar_arrive(SEMPTY(reg));
   };
 
+  // Warp-uniform probe: have the MMAs of tile j completed?
+  auto tile_done = [&](int j) -> bool {
+    return __all_sync(0xffffffffu, mbar_test(SFULL(NSR == 2 ? (j & 1) : 0), (j / NSR) & 1));
+  };
+
   float nk = 0.0f;
-  if (warp < 4) {
+#ifdef FGMM_EXP_TIMING
+  unsigned long long Ta = 0, Tb = 0, Tc = 0, Td = 0, Te = 0, Tx = globaltimer(), Tk0 = Tx;
+#define TICK(v) do { unsigned long long _t = globaltimer(); v += _t - Tx; Tx = _t; } while (0)
+#else
+#define TICK(v) do { } while (0)
+#endif
+  if (warp < kGammaWarps) {
     // ---------------- gamma warps
+    const int p0 = (warp >> 2) * 8;  // this warp's 8 points of each slice
     for (int s = 0; s < S && ok; ++s) {
-      // tile j is drained before this warp could need the MMA to have started tile j + NSR
-      while (nf < T && s >= kSlicesFlush * (nf + NSR) + kGBufs && ok) flush_next();
+      // Tile j is drained once this warp is kGBufs slices into tile j + 1: having waited
+      // for the MMAs of slice 8j + 7 it finds tile j complete, and the drain comes before
+      // this warp could need the MMA to have started tile j + NSR.
+      while (nf < T && s >= kSlicesFlush * (nf + 1) + kGBufs && ok) flush_next(false);
+      if (nf < T && s >= kSlicesFlush * (nf + 1) && tile_done(nf)) flush_next(false);  // early
+      TICK(Td);
       const int st = s % NST, gb = s % kGBufs;
-      ok = ok && __all_sync(0xffffffffu, mbar_wait(FULL(st), (s / NST) & 1, kErrWaitFull) &&
-                                             mbar_wait(GEMPTY(gb), ((s / kGBufs) & 1) ^ 1, kErrWaitGammaEmpty));
+      ok = ok && __all_sync(0xffffffffu, mbar_wait(FULL(st), (s / NST) & 1, kErrWaitFull));
+      TICK(Ta);
+      ok = ok && __all_sync(0xffffffffu, mbar_wait(GEMPTY(gb), ((s / kGBufs) & 1) ^ 1, kErrWaitGammaEmpty));
+      TICK(Tb);
       if (!ok) break;
       tc_fence_after();
       const uint8_t *stg = smem + st * Sh::kStage;
       const float *Ls = reinterpret_cast<const float *>(stg + Sh::kLOff);
       const float4 *ln4 = reinterpret_cast<const float4 *>(stg + Sh::kNOff);
       const int64_t nb = (s0 + s) * kSlicePts;
-      const int live = N - nb < kSlicePts ? (int)(N - nb) : kSlicePts;
-      float gh[16], gl[16];
+      const int live = (N - nb < kSlicePts ? (int)(N - nb) : kSlicePts) - p0;
+      float gh[8], gl[8];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const float4 l4 = ln4[c];
+      for (int c = 0; c < 2; ++c) {
+        const float4 l4 = ln4[p0 / 4 + c];
         const float ln2[4] = {l4.x, l4.y, l4.z, l4.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int p = c * 4 + e;
-          const float g = p < live ? ex2(Ls[p * NC + cl] - ln2[e]) : 0.0f;
+          const float g = p < live ? ex2(Ls[(p0 + p) * NC + cl] - ln2[e]) : 0.0f;
           nk += g;
           gh[p] = to_tf32(g);
           gl[p] = to_tf32(g - gh[p]);
@@ -686,27 +711,32 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(EMPTY(st));  // this warp is done with the slice's L
-      const uint32_t ga = lane_tmem + kGBase + gb * kGCols;
-      tmem_st16(ga, gh);
-      tmem_st16(ga + kSlicePts, gl);
+      const uint32_t ga = lane_tmem + kGBase + gb * kGCols + p0;
+      tmem_st8(ga, gh);
+      tmem_st8(ga + kSlicePts, gl);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(GFULL(gb));
+      TICK(Tc);
     }
-  } else if (warp == 4) {
+  } else if (warp == kGammaWarps) {
     // ---------------- MMA warp
     constexpr uint32_t idesc = idesc_tf32(NC, KA, 0, 1);  // A from TMEM, B MN-major
     for (int s = 0; s < S && ok; ++s) {
       const int j = s / kSlicesFlush, reg = NSR == 2 ? (j & 1) : 0;
       const bool tile_first = s % kSlicesFlush == 0;
       if (tile_first && j >= NSR) {
-        while (nf <= j - NSR && ok) flush_next();
+        while (nf <= j - NSR && ok) flush_next(false);
+        TICK(Te);
         ok = ok && __all_sync(0xffffffffu, mbar_wait(SEMPTY(reg), ((j / NSR) & 1) ^ 1, kErrWaitStatsDone));
       }
+      TICK(Td);
       const int st = s % NST, gb = s % kGBufs;
-      ok = ok && __all_sync(0xffffffffu, mbar_wait(FULL(st), (s / NST) & 1, kErrWaitFull) &&
-                                             mbar_wait(GFULL(gb), (s / kGBufs) & 1, kErrWaitGammaFull));
+      ok = ok && __all_sync(0xffffffffu, mbar_wait(FULL(st), (s / NST) & 1, kErrWaitFull));
+      TICK(Ta);
+      ok = ok && __all_sync(0xffffffffu, mbar_wait(GFULL(gb), (s / kGBufs) & 1, kErrWaitGammaFull));
+      TICK(Tb);
       if (!ok) break;
       if (lane == 0) {
         tc_fence_after();
@@ -730,13 +760,14 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
         if (s % kSlicesFlush == kSlicesFlush - 1 || s == S - 1) mma_commit(SFULL(reg));
       }
       __syncwarp();
+      TICK(Tc);
     }
     if (lane == 0 && S > 0) {  // every MMA of this CTA has completed before the teardown
       mma_commit(DONE);
       mbar_wait_drain(DONE, 0);
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == kGammaWarps + 1) {
     // ---------------- producer warp
     if (lane == 0) {
       prefetch_tmap(&tm_fhi);
@@ -744,9 +775,13 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
       prefetch_tmap(&tm_l);
     }
     for (int s = 0; s < S && ok; ++s) {
-      while (nf < T && s >= kSlicesFlush * (nf + NSR) + NST && ok) flush_next();
+      // same rule as the gamma warps, NST slices ahead (before the EMPTY wait below)
+      while (nf < T && s >= kSlicesFlush * (nf + 1) + NST && ok) flush_next(false);
+      if (nf < T && s >= kSlicesFlush * (nf + 1) && tile_done(nf)) flush_next(false);  // early
       const int st = s % NST;
+      TICK(Td);
       if (s >= NST) ok = ok && __all_sync(0xffffffffu, mbar_wait(EMPTY(st), ((s / NST) & 1) ^ 1, kErrWaitEmpty));
+      TICK(Ta);
       if (!ok) break;
       if (lane == 0) {
         const uint32_t base = smem_u32(smem + st * Sh::kStage);
@@ -764,8 +799,9 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
       for (int s = (S > NST ? S - NST : 0); s < S; ++s) mbar_wait_drain(FULL(s % NST), (s / NST) & 1);
     __syncwarp();
   }
-  // every warp drains the tiles it has not drained yet
-  while (nf < T && ok) flush_next();
+  // every warp drains the tiles it has not drained yet (the drain-only warps sleep between
+  // polls)
+  while (nf < T && ok) flush_next(warp > kGammaWarps + 1);
 
   ok = cta_sync_and(ok);
   const int k = ct * NC + cl;
@@ -778,14 +814,25 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
       *reinterpret_cast<float4 *>(o) = ok ? make_float4(sacc[e], sacc[e + 1], sacc[e + 2], sacc[e + 3])
                                           : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    if (warp < 4) dst[2 * DP] = ok ? nk : 0.0f;
   }
+  // n_k: the two gamma warps of a lane quarter add up their halves of the points
+  float *nk_s = reinterpret_cast<float *>(smem);  // [128], the stage ring is idle now
+  if (warp >= 4 && warp < kGammaWarps) nk_s[cl] = nk;
+  __syncthreads();
+  if (warp < 4 && k < K)
+    partial[((int64_t)slot * K + k) * PSTRIDE + 2 * DP] = ok ? nk + nk_s[cl] : 0.0f;
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+#ifdef FGMM_EXP_TIMING
+  if (lane == 0 && (warp == 0 || warp == kGammaWarps || warp == kGammaWarps + 1) && blockIdx.x < 512) {
+    unsigned long long *o = g_tim[blockIdx.x * 4 + (warp == 0 ? 0 : warp - kGammaWarps + 1)];
+    o[0] = Ta; o[1] = Tb; o[2] = Tc; o[3] = Td; o[4] = Te; o[5] = 0; o[6] = globaltimer() - Tk0; o[7] = S;
+  }
+#endif
 }
 
 // ------------------------------------------------------------------------- host

@@ -74,6 +74,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe: has the phase with the given parity completed?
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity to complete.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int err_code) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -81,6 +93,24 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int err
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0) {
+      if (*(volatile int *)&g_dev_error != 0) return false;
+      if (globaltimer() - t0 > kWaitNs) {
+        atomicCAS(&g_dev_error, 0, err_code);
+        return false;
+      }
+    }
+  }
+}
+
+// Bounded wait for waits off the critical path: polls with a short sleep in between, so a
+// warp that has nothing to do until the phase completes leaves the issue slots to others.
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, int err_code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    __nanosleep(64);
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 0) {
       if (*(volatile int *)&g_dev_error != 0) return false;
       if (globaltimer() - t0 > kWaitNs) {
         atomicCAS(&g_dev_error, 0, err_code);
