@@ -213,14 +213,13 @@ __device__ __forceinline__ bool drain_group(uint32_t lane_tmem, uint32_t &gcount
   if (!__all_sync(0xffffffffu, mbar_wait(tfull0 + 8u * buf, use & 1u, kErrWaitTmemFull)))
     return false;
   tc_fence_after();
+  float v[kHalf];  // all loads in flight before the one wait
 #pragma unroll
-  for (int h = 0; h < kHalf / 16; ++h) {
-    float v[16];
-    tmem_ld16(lane_tmem + buf * NC + h * 16, v);
-    tmem_wait_ld();
+  for (int h = 0; h < kHalf / 32; ++h)
+    tmem_ld32(lane_tmem + buf * NC + h * 32, *reinterpret_cast<float(*)[32]>(v + h * 32));
+  tmem_wait_ld();
 #pragma unroll
-    for (int e = 0; e < 16; ++e) acc[h * 16 + e] = kFirst ? v[e] : acc[h * 16 + e] + v[e];
-  }
+  for (int e = 0; e < kHalf; ++e) acc[e] = kFirst ? v[e] : acc[e] + v[e];
   tc_fence_before();
   __syncwarp();
   if (lane == 0) mbar_arrive(tempty0 + 8u * buf);
@@ -431,7 +430,7 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
 // block.
 // Eight lanes per point (four points per warp), lanes striped over the dimensions; all
 // loads of a point are issued before its reductions.
-template <int DPL>  // dimensions per lane: ceil(d / 8)
+template <int DPL, bool VEC>  // dimensions per lane: ceil(d / 8); VEC: float4 loads
 __global__ void __launch_bounds__(256)
 tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__restrict__ sc,
                  const float *__restrict__ ms, const float *__restrict__ lc,
@@ -471,17 +470,38 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
     if (j2 >= 0 && b2 < b1 - 40.0f) j2 = -1;
     const int k1 = j1 >= 0 ? j1 : 0, k2 = j2 >= 0 ? j2 : 0;
     const bool need2 = __any_sync(0xffffffffu, j2 >= 0);
+    // lane `sub` takes the DPL consecutive dimensions starting at sub * DPL
     float x[DPL], s1[DPL], m1[DPL], s2[DPL], m2[DPL];
+    const bool use2 = need2 && j2 >= 0;
+    const int j0 = sub * DPL;
+    if (VEC) {  // d == 8 DPL, DPL % 4 == 0, 16-byte aligned rows
+      const float4 *xp = reinterpret_cast<const float4 *>(X + nn * d + j0);
+      const float4 *s1p = reinterpret_cast<const float4 *>(sc + (int64_t)k1 * d + j0);
+      const float4 *m1p = reinterpret_cast<const float4 *>(ms + (int64_t)k1 * d + j0);
+      const float4 *s2p = reinterpret_cast<const float4 *>(sc + (int64_t)k2 * d + j0);
+      const float4 *m2p = reinterpret_cast<const float4 *>(ms + (int64_t)k2 * d + j0);
 #pragma unroll
-    for (int i = 0; i < DPL; ++i) {
-      const int j = sub + 8 * i;
-      const bool in = j < d;
-      x[i] = in ? __ldg(X + nn * d + j) : 0.0f;
-      s1[i] = in ? __ldg(sc + (int64_t)k1 * d + j) : 0.0f;
-      m1[i] = in ? __ldg(ms + (int64_t)k1 * d + j) : 0.0f;
-      const bool in2 = in && need2 && j2 >= 0;
-      s2[i] = in2 ? __ldg(sc + (int64_t)k2 * d + j) : 0.0f;
-      m2[i] = in2 ? __ldg(ms + (int64_t)k2 * d + j) : 0.0f;
+      for (int i = 0; i < DPL / 4; ++i) {
+        const float4 a = __ldg(xp + i), b = __ldg(s1p + i), c = __ldg(m1p + i);
+        const float4 e = use2 ? __ldg(s2p + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 f = use2 ? __ldg(m2p + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        x[4 * i] = a.x; x[4 * i + 1] = a.y; x[4 * i + 2] = a.z; x[4 * i + 3] = a.w;
+        s1[4 * i] = b.x; s1[4 * i + 1] = b.y; s1[4 * i + 2] = b.z; s1[4 * i + 3] = b.w;
+        m1[4 * i] = c.x; m1[4 * i + 1] = c.y; m1[4 * i + 2] = c.z; m1[4 * i + 3] = c.w;
+        s2[4 * i] = e.x; s2[4 * i + 1] = e.y; s2[4 * i + 2] = e.z; s2[4 * i + 3] = e.w;
+        m2[4 * i] = f.x; m2[4 * i + 1] = f.y; m2[4 * i + 2] = f.z; m2[4 * i + 3] = f.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) {
+        const int j = j0 + i;
+        const bool in = j < d;
+        x[i] = in ? __ldg(X + nn * d + j) : 0.0f;
+        s1[i] = in ? __ldg(sc + (int64_t)k1 * d + j) : 0.0f;
+        m1[i] = in ? __ldg(ms + (int64_t)k1 * d + j) : 0.0f;
+        s2[i] = in && use2 ? __ldg(sc + (int64_t)k2 * d + j) : 0.0f;
+        m2[i] = in && use2 ? __ldg(ms + (int64_t)k2 * d + j) : 0.0f;
+      }
     }
     float p1 = 0.0f, p2 = 0.0f;
 #pragma unroll
@@ -649,12 +669,20 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
     if (!ok) return;
     tc_fence_after();
 #pragma unroll
-    for (int c = 0; c < SEG / 16; ++c) {
-      float v[16];
-      tmem_ld16(lane_tmem + reg * KA + seg * SEG + c * 16, v);
+    for (int c = 0; c < SEG / 32; ++c) {  // two loads in flight per wait
+      float v[32];
+      tmem_ld16(lane_tmem + reg * KA + seg * SEG + c * 32, *reinterpret_cast<float(*)[16]>(v));
+      tmem_ld16(lane_tmem + reg * KA + seg * SEG + c * 32 + 16, *reinterpret_cast<float(*)[16]>(v + 16));
       tmem_wait_ld();
 #pragma unroll
-      for (int e = 0; e < 16; ++e) sacc[c * 16 + e] += v[e];
+      for (int e = 0; e < 32; ++e) sacc[c * 32 + e] += v[e];
+    }
+    if (SEG % 32) {
+      float v[16];
+      tmem_ld16(lane_tmem + reg * KA + seg * SEG + SEG - 16, v);
+      tmem_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 16; ++e) sacc[SEG - 16 + e] += v[e];
     }
     tc_fence_before();
     __syncwarp();
@@ -975,10 +1003,19 @@ int tc_launch(const TcPlan &p, const float *X, const float *pts, const TcWs &w, 
   {
     const int blocks = refine_blocks(p.N);
     const int dpl = (p.d + 7) / 8;
+    const bool vec = p.d % 32 == 0 && reinterpret_cast<uintptr_t>(X) % 16 == 0;  // d = 8 DPL
 #define FGMM_REFINE(D)                                                                          \
-  tc_refine_kernel<D><<<blocks, 256, 0, st>>>(X, p.N, p.d, w.sc, w.ms, w.lc, w.part_m, w.part_s, \
-                                              w.part_tv, w.part_ti, p.G, w.ln2x, w.L, p.Kp,     \
-                                              ln, w.ln_part)
+  do {                                                                                          \
+    if (vec && (D) % 4 == 0 && 8 * (D) == p.d)                                                  \
+      tc_refine_kernel<D, true><<<blocks, 256, 0, st>>>(X, p.N, p.d, w.sc, w.ms, w.lc, w.part_m, \
+                                                        w.part_s, w.part_tv, w.part_ti, p.G,     \
+                                                        w.ln2x, w.L, p.Kp, ln, w.ln_part);       \
+    else                                                                                        \
+      tc_refine_kernel<D, false><<<blocks, 256, 0, st>>>(X, p.N, p.d, w.sc, w.ms, w.lc,          \
+                                                         w.part_m, w.part_s, w.part_tv,          \
+                                                         w.part_ti, p.G, w.ln2x, w.L, p.Kp, ln,  \
+                                                         w.ln_part);                             \
+  } while (0)
     if (dpl <= 1) FGMM_REFINE(1);
     else if (dpl <= 2) FGMM_REFINE(2);
     else if (dpl <= 4) FGMM_REFINE(4);

@@ -10,56 +10,71 @@ namespace fgmm {
 
 // partials: [slots][K][W] fp32, each row laid out [s (ds) | sq (ds) | n | ...] where only
 // the first d of each ds-wide run are meaningful; stats: [n (K) | s (K d) | sq (K d) | sum ln].
-// One thread per output value; the slots are summed in a fixed order with eight
-// independent loads in flight (deterministic).  Block 0 also sums the per-block
+// A block takes 32 consecutive output values (lane = value, so the loads of a warp are
+// contiguous) and splits the slots over its 8 warps (warp g sums slots g, g + 8, ... with
+// every load in flight before the adds); the 8 warp sums are then added in a fixed order,
+// so the result does not depend on timing.  Block 0 also sums the per-block
 // log-normalizer partials into the last entry.
-__global__ void reduce_partials_kernel(const float *__restrict__ part, int slots, int K, int d,
-                                       int ds, int W, const double *__restrict__ lnp, int ln_slots,
-                                       double *__restrict__ stats) {
+constexpr int kRedGroups = 8;
+constexpr int kRedUnroll = 16;  // loads in flight per thread (one round trip up to 128 slots)
+__global__ void __launch_bounds__(32 * kRedGroups)
+reduce_partials_kernel(const float *__restrict__ part, int slots, int K, int d, int ds, int W,
+                       const double *__restrict__ lnp, int ln_slots, double *__restrict__ stats) {
+  __shared__ double sh[kRedGroups][32];
   const int V = 2 * d + 1;
   const int64_t total = (int64_t)K * V;
   const int64_t slot_stride = (int64_t)K * W;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int k = (int)(i / V), c = (int)(i % V);
-    int src;
-    int64_t dst;
-    if (c < d)          { src = c;               dst = K + (int64_t)k * d + c; }
-    else if (c < 2 * d) { src = ds + (c - d);    dst = K + (int64_t)K * d + (int64_t)k * d + (c - d); }
-    else                { src = 2 * ds;          dst = k; }
+  const int lane = threadIdx.x & 31, g = threadIdx.x >> 5;
+  for (int64_t base = (int64_t)blockIdx.x * 32; base < total; base += (int64_t)gridDim.x * 32) {
+    const int64_t i = base + lane;
+    const bool live = i < total;
+    const int k = live ? (int)(i / V) : 0, c = live ? (int)(i % V) : 0;
+    const int src = c < d ? c : (c < 2 * d ? ds + (c - d) : 2 * ds);
     const float *p = part + (int64_t)k * W + src;
     double acc = 0.0;
-    int s = 0;
-    for (; s + 8 <= slots; s += 8) {
-      float v[8];
+    for (int s = g; s < slots; s += kRedUnroll * kRedGroups) {  // all loads, then the adds
+      float v[kRedUnroll];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = __ldg(p + (int64_t)(s + u) * slot_stride);
+      for (int u = 0; u < kRedUnroll; ++u) {
+        const int ss = s + u * kRedGroups;
+        v[u] = (live && ss < slots) ? __ldg(p + (int64_t)ss * slot_stride) : 0.0f;
+      }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) acc += (double)v[u];
+      for (int u = 0; u < kRedUnroll; ++u) acc += (double)v[u];
     }
-    for (; s < slots; ++s) acc += (double)__ldg(p + (int64_t)s * slot_stride);
-    stats[dst] = acc;
+    sh[g][lane] = acc;
+    __syncthreads();
+    if (g == 0 && live) {
+      double t = 0.0;
+#pragma unroll
+      for (int u = 0; u < kRedGroups; ++u) t += sh[u][lane];
+      const int64_t dst = c < d ? K + (int64_t)k * d + c
+                        : (c < 2 * d ? K + (int64_t)K * d + (int64_t)k * d + (c - d) : (int64_t)k);
+      stats[dst] = t;
+    }
+    __syncthreads();
   }
   if (blockIdx.x == 0) {
-    __shared__ double sh[256];
     double a = 0.0;
     for (int j = threadIdx.x; j < ln_slots; j += blockDim.x) a += lnp[j];
-    sh[threadIdx.x] = a;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    if (lane == 0) sh[g][0] = a;
     __syncthreads();
-    for (int o = blockDim.x / 2; o > 0; o >>= 1) {
-      if (threadIdx.x < o) sh[threadIdx.x] += sh[threadIdx.x + o];
-      __syncthreads();
+    if (threadIdx.x == 0) {
+      double t = 0.0;
+      for (int u = 0; u < kRedGroups; ++u) t += sh[u][0];
+      stats[total] = t;
     }
-    if (threadIdx.x == 0) stats[total] = sh[0];
   }
 }
 
 int reduce_partials(const float *partials, int slots, int K, int d, int ds, int W,
                     const double *ln_partials, int ln_slots, double *stats, cudaStream_t stream) {
   const int64_t total = (int64_t)K * (2 * d + 1);
-  int blocks = (int)std::min<int64_t>(cdiv(total, 256), 8 * num_sms());
-  reduce_partials_kernel<<<blocks, 256, 0, stream>>>(partials, slots, K, d, ds, W, ln_partials,
-                                                     ln_slots, stats);
+  int blocks = (int)std::min<int64_t>(cdiv(total, 32), 16 * num_sms());
+  reduce_partials_kernel<<<blocks, 32 * kRedGroups, 0, stream>>>(partials, slots, K, d, ds, W,
+                                                                 ln_partials, ln_slots, stats);
   FGMM_LAUNCH_CHECK("reduce_partials_kernel");
   mark(stream, "reduce_partials_kernel");
   return FGMM_OK;
