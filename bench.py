@@ -14,7 +14,8 @@ ranks per second.
 Rank 0 prints ONE JSON line.  Besides the contract keys it carries ``roofline``
 (dominant kernel, CUDA-event timed inside this run), ``cpu_baseline`` (the
 reference's own C++/OpenMP op on this host's cores, N=1 only), ``e2e`` (whole
-``NativeFlashGMM.fit`` calls from pinned host memory), ``clocks`` (nvidia-smi
+EM iterations through the public op with every step's inputs copied from pinned host
+memory and its results read back), ``clocks`` (nvidia-smi
 sampled during the timed region) and ``gpu_launches``.
 
 ``--impl reference`` times the reference's CPU implementation of the same step
@@ -38,7 +39,6 @@ import torch.distributed as dist  # noqa: E402
 
 from flashgmm_b200.data import WORKLOADS, make_workload  # noqa: E402
 
-FIT_ITERS = 20
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 
 
@@ -57,11 +57,31 @@ def peaks():
 
 
 def algorithmic(wl, n_points):
-    """Per-iteration contraction FLOPs (12 N K d) and minimum HBM bytes
-    4 (N d + N + 4 K d + 2 K)."""
-    flops = 12.0 * n_points * wl.K * wl.d
-    nbytes = 4.0 * (n_points * wl.d + n_points + 4 * wl.K * wl.d + 2 * wl.K)
+    """Per-iteration algorithmic work of the tensor-core path.
+
+    FLOPs: the two contractions, each 2 N K (2 d) multiply-adds counted as fp32 products
+    (distance GEMM [x^2 | x] . [1/var | -2 mu/var], statistics GEMM gamma^T [x^2 | x]):
+    8 N K d.  Bytes: X read by pass 1, the refine and the statistics pass (3 N d), the
+    log2-likelihood matrix L written once and read once (2 N K), per-point scalars and
+    the parameters (4 N + 4 K d + 2 K), all fp32."""
+    N, K, d = n_points, wl.K, wl.d
+    flops = 8.0 * N * K * d
+    nbytes = 4.0 * (3 * N * d + 2 * N * K + 4 * N + 4 * K * d + 2 * K)
     return flops, nbytes
+
+
+def ncu_traffic(kernel, workload):
+    """DRAM bytes per launch (read + write) of `kernel` on `workload` from the committed
+    ncu summary profiles/ncu_traffic.txt (lines: kernel workload bytes), or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "ncu_traffic.txt")) as f:
+            for ln in f:
+                p = ln.split()
+                if len(p) >= 3 and not ln.startswith("#") and p[0] == kernel and p[1] == workload:
+                    return float(p[2])
+    except OSError:
+        pass
+    return None
 
 
 class ClockSampler:
@@ -305,21 +325,22 @@ def run_ours(args, wl):
     pk = peaks()
     tf32_eff = pk["bf16_tflops"] / 2.0 / 3.0  # 3xTF32: three TF32 products per fp32 product
     flops, nbytes = algorithmic(wl, N)
-    # the dominant kernel's share of the algorithmic work (pass 1: 4NKd, pass 2: 8NKd)
-    if "pass1" in dom:
-        f_dom = flops / 3.0
-    elif "pass2" in dom:
-        f_dom = flops * 2.0 / 3.0
+    gemm = dom in ("tc_pass1_kernel", "tc_stats_kernel")
+    if gemm:  # each of the two kernels carries one of the two contractions
+        achieved = flops / 2.0 / (prof[dom] * 1e-3) / 1e12
+        roofline = {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": tf32_eff,
+                    "unit": "TFLOP/s", "frac": achieved / tf32_eff}
     else:
-        f_dom = flops
-    achieved = f_dom / (prof[dom] * 1e-3) / 1e12
-    roofline = {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": tf32_eff,
-                "unit": "TFLOP/s", "frac": achieved / tf32_eff, "traffic": None,
-                "kernel_ms": prof[dom], "launch_ms": prof,
-                "peak_note": (f"3xTF32 effective = {pk['source']} bf16 {pk['bf16_tflops']:.0f} TF/s"
-                              " / 2 (tf32) / 3 (products)"),
-                "iteration_frac": (flops / (ms_per_step * 1e-3) / 1e12) / tf32_eff,
-                "algorithmic": {"flops_per_iter": flops, "bytes_per_iter": nbytes}}
+        achieved = nbytes / (prof[dom] * 1e-3) / 1e9
+        roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": pk["hbm_gbs"],
+                    "unit": "GB/s", "frac": achieved / pk["hbm_gbs"]}
+    roofline.update({
+        "traffic": ncu_traffic(dom, wl.name), "kernel_ms": prof[dom], "launch_ms": prof,
+        "peak_note": (f"3xTF32 effective = {pk['source']} bf16 {pk['bf16_tflops']:.0f} TF/s / 2 "
+                      f"(tf32) / 3 (products); hbm {pk['source']} {pk['hbm_gbs']:.0f} GB/s"),
+        "iteration_frac": (flops / (ms_per_step * 1e-3) / 1e12) / tf32_eff,
+        "algorithmic": {"flops_per_iter": flops, "bytes_per_iter": nbytes,
+                        "dominant_flops_per_launch": flops / 2.0 if gemm else None}})
 
     launches = lib.fgmm_em_stats_launches(N, d, K) + 1
     e2e = None
@@ -348,51 +369,78 @@ def run_ours(args, wl):
         dist.destroy_process_group()
 
 
-def run_e2e(wl, dev, args, ws_n=1, rank=0):
-    """Whole fits through the public API from pinned host memory: H2D of this rank's X
-    shard and the initial parameters, FIT_ITERS EM iterations (NativeFlashGMM on one GPU,
-    DistributedFlashGMM with the stats all_reduce on several), D2H of the fitted
-    parameters.  Wall clock, max over ranks; value counts workload-sized iterations of all
-    ranks per second (weak scaling, like ``value``)."""
+def run_e2e(wl, dev, args, ws_n=1, rank=0, steps=200):
+    """The same metric through the public API from HOST buffers.  Every step copies this
+    rank's X shard and the current parameters from pinned host memory to the GPU, runs one
+    EM iteration (``flash_gmm_native.flash_em_fused`` on one GPU; ``em_stats`` +
+    ``all_reduce`` + ``em_update`` on several) and reads the new parameters and the log
+    normaliser back into pinned host memory.  The X copy of step i + 1 runs on a second
+    stream into a second device buffer while step i computes.  Wall clock over `steps`
+    steps after a warm-up, max over ranks; value counts workload-sized iterations of all
+    ranks per second."""
+    from flashgmm_b200 import flash_gmm_native as C
     n_total = wl.N * ws_n
     X, mu, var, lp = make_workload(wl, N=n_total, rows=(rank * wl.N, (rank + 1) * wl.N))
     Xh = X.pin_memory()
-    init_h = [t.pin_memory() for t in (mu, var, lp)]
-    if ws_n > 1:
-        from flashgmm_b200.distributed import DistributedFlashGMM
-        m = DistributedFlashGMM(K=wl.K, d=wl.d, max_iter=FIT_ITERS, tol=0.0)
-    else:
-        from flashgmm_b200.native_wrapper import NativeFlashGMM
-        m = NativeFlashGMM(K=wl.K, d=wl.d, max_iter=FIT_ITERS, tol=0.0, device=dev)
+    ph = [t.pin_memory() for t in (mu, var, lp)]
+    N, d, K = wl.N, wl.d, wl.K
+    Xd = [torch.empty_like(X, device=dev) for _ in range(2)]
+    pd = [torch.empty_like(t, device=dev) for t in ph]
+    out_h = [torch.empty_like(t).pin_memory() for t in ph] + [torch.empty(N).pin_memory()]
+    copy = torch.cuda.Stream(dev)
+    comp = torch.cuda.current_stream(dev)
+    landed = [torch.cuda.Event() for _ in range(2)]
+    freed = [torch.cuda.Event() for _ in range(2)]
+    ws = C.StatsWorkspace(N, d, K, dev) if ws_n > 1 else None
 
-    def one():
-        Xd = Xh.to(dev, non_blocking=True)
-        init = [t.to(dev, non_blocking=True) for t in init_h]
+    def issue_copy(i):
+        b = i % 2
+        with torch.cuda.stream(copy):
+            copy.wait_event(freed[b])
+            Xd[b].copy_(Xh, non_blocking=True)
+            landed[b].record(copy)
+
+    def step(i):
+        b = i % 2
+        comp.wait_event(landed[b])
+        for t, h in zip(pd, ph):
+            t.copy_(h, non_blocking=True)
         if ws_n > 1:
-            m.fit(Xd, init)
+            stats, ln = C.em_stats(Xd[b], pd[0], pd[1], pd[2], workspace=ws)
+            dist.all_reduce(stats)
+            out = list(C.em_update(stats, n_total, K, d)) + [ln]
         else:
-            m.fit(Xd, init=init)
-        return [m.mu.cpu(), m.var.cpu(), m.log_pi.cpu()]
+            out = C.flash_em_fused(Xd[b], pd[0], pd[1], pd[2])
+        freed[b].record(comp)
+        for h, t in zip(out_h, out):
+            h.copy_(t, non_blocking=True)
 
-    one()
-    reps = 3
-    torch.cuda.synchronize()
+    def run(n):
+        issue_copy(0)
+        for i in range(n):
+            if i + 1 < n:
+                issue_copy(i + 1)
+            step(i)
+        torch.cuda.synchronize(dev)
+
+    run(3)
     if ws_n > 1:
         dist.barrier()
     t0 = time.perf_counter()
-    for _ in range(reps):
-        out = one()
-    dt = (time.perf_counter() - t0) / reps
+    run(steps)
+    dt = (time.perf_counter() - t0) / steps
     if ws_n > 1:
         t = torch.tensor([dt], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dt = t.item()
-    h2d = Xh.numel() * 4 + sum(t.numel() * 4 for t in init_h)
-    d2h = sum(t.numel() * 4 for t in out) + 8 * FIT_ITERS
-    return {"value": ws_n * FIT_ITERS / dt, "unit": "iter/s", "h2d_bytes_per_step": h2d,
+    h2d = Xh.numel() * 4 + sum(t.numel() * 4 for t in ph)
+    d2h = sum(t.numel() * 4 for t in out_h)
+    return {"value": ws_n / dt, "unit": "iter/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
-            "step": (f"{'DistributedFlashGMM' if ws_n > 1 else 'NativeFlashGMM'}.fit of "
-                     f"{FIT_ITERS} iterations from pinned host X (wall clock, per-rank bytes)")}
+            "step": ("H2D of X and the parameters from pinned host memory, one EM iteration "
+                     "through flashgmm_b200.flash_gmm_native, D2H of the new parameters and "
+                     "log-normalizer; X copies double-buffered on a second stream (per-rank "
+                     "bytes)")}
 
 
 def main():

@@ -228,6 +228,12 @@ __device__ __forceinline__ bool drain_group(uint32_t lane_tmem, uint32_t &gcount
 }
 
 // ------------------------------------------------------------------------- pass 1
+#ifdef FGMM_EXP_TIMING1
+__device__ unsigned long long g_tim1[2048][8];
+#define T1TICK(v) do { unsigned long long _t = globaltimer(); v += _t - Tx1; Tx1 = _t; } while (0)
+#else
+#define T1TICK(v) do { } while (0)
+#endif
 template <int NKC>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ CUtensorMap tm_plo,
@@ -235,7 +241,7 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
                 const float *__restrict__ cst2, int64_t N, int n_pt, int n_ct, int G, int tpg,
                 float *__restrict__ part_m, float *__restrict__ part_s,
                 float2 *__restrict__ part_tv, int2 *__restrict__ part_ti,
-                float *__restrict__ Lout, int Kp) {
+                float *__restrict__ Lt, int64_t Npad) {
   constexpr int S = kStages1;
   constexpr int NB = 4;  // TMEM group buffers (4 x 128 columns)
   extern __shared__ uint8_t smem_raw[];
@@ -270,6 +276,9 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int n_units = n_pt * G;
+#ifdef FGMM_EXP_TIMING1
+  unsigned long long A1 = 0, B1 = 0, C1 = 0, D1 = 0, Tx1 = globaltimer(), T01 = Tx1;
+#endif
 
   if (warp == 0) {
     if (lane == 0) {
@@ -282,7 +291,9 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
         const int t1 = min(n_ct, (g + 1) * tpg);
         for (int t = g * tpg; t < t1 && ok; ++t) {
           for (int c = 0; c < NKC; ++c) {
+            T1TICK(B1);
             if (!mbar_wait(EMPTY(stage), phase ^ 1, kErrWaitEmpty)) { ok = false; break; }
+            T1TICK(A1);
             const uint32_t base = smem_u32(smem + stage * kStageBytes);
             mbar_arrive_expect_tx(FULL(stage), kStageBytes);
             tma_load_2d(base, &tm_phi, c * KC, pt * BM, FULL(stage));
@@ -309,12 +320,15 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
         const int t1 = min(n_ct, (g + 1) * tpg);
         for (int t = g * tpg; t < t1 && ok; ++t) {
           for (int c = 0; c < NKC; ++c) {
+            T1TICK(D1);
             if (!mbar_wait(FULL(stage), phase, kErrWaitFull)) { ok = false; break; }
+            T1TICK(A1);
             tc_fence_after();
             constexpr int GC = group_chunks<NKC>();
             if (!issue_dist_chunk<NB>(smem_u32(smem + stage * kStageBytes), tmem, gcount, TFULL0,
                                       TEMPTY0, c % GC == 0, c % GC == GC - 1)) { ok = false; break; }
             mma_commit(EMPTY(stage));
+            T1TICK(B1);
             if (++stage == S) { stage = 0; phase ^= 1; }
           }
         }
@@ -338,10 +352,13 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
       const int64_t n_row = (int64_t)pt * BM + row;
       for (int t = g * tpg; t < t1 && ok; ++t) {
         float acc[kHalf];
+        T1TICK(D1);
         ok = drain_group<NB, true>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
+        T1TICK(C1);
 #pragma unroll 1
         for (int grp = 1; grp < NKC / group_chunks<NKC>() && ok; ++grp)
           ok = drain_group<NB, false>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
+        T1TICK(A1);
         if (!ok) break;
         const float *cp = cst2 + (int64_t)t * NC + half * kHalf;
 #pragma unroll
@@ -352,12 +369,11 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
             acc[j * 32 + e] = fmaf(acc[j * 32 + e], -0.5f * kLog2e, __ldg(cp + j * 32 + e));
             cm = fmaxf(cm, acc[j * 32 + e]);
           }
-          if (n_row < N) {  // the log2-likelihood matrix L feeds the statistics pass
-            float4 *lp = reinterpret_cast<float4 *>(Lout + n_row * Kp + t * NC + half * kHalf + j * 32);
+          {  // the log2-likelihood matrix feeds the statistics pass; stored transposed
+             // (Lt [component][point]) so that each store of a warp is 32 consecutive points
+            float *lp = Lt + (int64_t)(t * NC + half * kHalf + j * 32) * Npad + n_row;
 #pragma unroll
-            for (int e = 0; e < 8; ++e)
-              lp[e] = make_float4(acc[j * 32 + 4 * e], acc[j * 32 + 4 * e + 1],
-                                  acc[j * 32 + 4 * e + 2], acc[j * 32 + 4 * e + 3]);
+            for (int e = 0; e < 32; ++e) lp[(int64_t)e * Npad] = acc[j * 32 + e];
           }
           const float mn = fmaxf(m, cm);
           const float mr = (mn == -INFINITY) ? 0.0f : mn;
@@ -379,6 +395,7 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
           }
         }
       }
+      T1TICK(B1);
       // merge the two column halves of each row
       if (half == 1) lse_x[row] = Half{m, s, v1, v2, i1, i2};
       ok = epi_sync_and(ok);
@@ -415,6 +432,12 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+#ifdef FGMM_EXP_TIMING1
+  if (lane == 0 && warp < 4 && blockIdx.x < 512) {
+    unsigned long long *o = g_tim1[blockIdx.x * 4 + warp];
+    o[0] = A1; o[1] = B1; o[2] = C1; o[3] = D1; o[6] = globaltimer() - T01; o[7] = 1;
+  }
+#endif
 }
 
 // ------------------------------------------------------------------------- refine
@@ -436,7 +459,7 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
                  const float *__restrict__ ms, const float *__restrict__ lc,
                  const float *__restrict__ part_m, const float *__restrict__ part_s,
                  const float2 *__restrict__ part_tv, const int2 *__restrict__ part_ti, int G,
-                 float *__restrict__ ln2x, float *__restrict__ L, int Kp,
+                 float *__restrict__ ln2x, float *__restrict__ Lt, int64_t Npad,
                  float *__restrict__ ln_out, double *__restrict__ ln_part) {
   __shared__ double wsum[8];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -529,8 +552,8 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
     const float ln2 = m + __log2f(tot);
     if (live && sub == 0) {
       ln2x[n] = ln2;
-      if (j1 >= 0) L[n * Kp + j1] = e1;
-      if (j2 >= 0) L[n * Kp + j2] = e2;
+      if (j1 >= 0) Lt[(int64_t)j1 * Npad + n] = e1;
+      if (j2 >= 0) Lt[(int64_t)j2 * Npad + n] = e2;
       const float l = ln2 * kLn2;
       ln_out[n] = l;
       acc += (double)l;
@@ -581,7 +604,7 @@ template <int KA>
 struct StatsShape {
   static constexpr int kAtom = kSlicePts * 128;                // 2 KB: 16 points x 32 fp32
   static constexpr int kFPart = (KA / 32) * kAtom;             // F hi (or lo) of a slice
-  static constexpr int kLOff = 2 * kFPart;                     // L tile [16][128]
+  static constexpr int kLOff = 2 * kFPart;                     // L tile [128][16], 64B-swizzled
   static constexpr int kNOff = kLOff + kSlicePts * NC * 4;     // ln2 [16]
   static constexpr int kStage = (kNOff + kSlicePts * 4 + 1023) / 1024 * 1024;
   static constexpr int kStagesFit = (220 * 1024) / kStage;
@@ -719,7 +742,10 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
       if (!ok) break;
       tc_fence_after();
       const uint8_t *stg = smem + st * Sh::kStage;
-      const float *Ls = reinterpret_cast<const float *>(stg + Sh::kLOff);
+      // this lane's component row of the L tile: 16 points = four 16-byte chunks, chunk c
+      // stored at c ^ ((row >> 1) & 3) (SWIZZLE_64B)
+      const float4 *Lrow = reinterpret_cast<const float4 *>(stg + Sh::kLOff + cl * 64);
+      const int sw = (cl >> 1) & 3;
       const float4 *ln4 = reinterpret_cast<const float4 *>(stg + Sh::kNOff);
       const int64_t nb = (s0 + s) * kSlicePts;
       const int live = (N - nb < kSlicePts ? (int)(N - nb) : kSlicePts) - p0;
@@ -727,11 +753,13 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const float4 l4 = ln4[p0 / 4 + c];
+        const float4 v4 = Lrow[(p0 / 4 + c) ^ sw];
         const float ln2[4] = {l4.x, l4.y, l4.z, l4.w};
+        const float lv[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int p = c * 4 + e;
-          const float g = p < live ? ex2(Ls[(p0 + p) * NC + cl] - ln2[e]) : 0.0f;
+          const float g = p < live ? ex2(lv[e] - ln2[e]) : 0.0f;
           nk += g;
           gh[p] = to_tf32(g);
           gl[p] = to_tf32(g - gh[p]);
@@ -817,7 +845,7 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
         mbar_arrive_expect_tx(FULL(st), 2 * Sh::kFPart + kSlicePts * NC * 4 + kSlicePts * 4);
         tma_load_3d(base, &tm_fhi, 0, (int32_t)nb, 0, FULL(st));
         tma_load_3d(base + Sh::kFPart, &tm_flo, 0, (int32_t)nb, 0, FULL(st));
-        tma_load_2d(base + Sh::kLOff, &tm_l, ct * NC, (int32_t)nb, FULL(st));
+        tma_load_2d(base + Sh::kLOff, &tm_l, (int32_t)nb, ct * NC, FULL(st));
         bulk_load(base + Sh::kNOff, ln2x + nb, kSlicePts * 4, FULL(st));
       }
       __syncwarp();
@@ -925,7 +953,11 @@ TcPlan plan(int64_t N, int d, int K) {
   p.Kp = p.n_ct * NC;
   p.n_pt = (int)cdiv(N, BM);
   const int sms = num_sms();
+#ifndef FGMM_G_OVERRIDE
   int G = (int)std::min<int64_t>(p.n_ct, std::max<int64_t>(1, cdiv(4 * sms, p.n_pt)));
+#else
+  int G = (int)std::min<int64_t>(p.n_ct, std::max<int64_t>(1, cdiv(FGMM_G_OVERRIDE * sms, p.n_pt)));
+#endif
   p.tpg = (int)cdiv(p.n_ct, G);
   p.G = (int)cdiv(p.n_ct, p.tpg);
   p.grid1 = (int)std::min<int64_t>((int64_t)p.n_pt * p.G, sms);
@@ -961,7 +993,7 @@ TcWs tc_layout(void *ws, const TcPlan &p) {
   w.ln2x = c.take<float>(p.N);
   w.partial = c.take<float>((size_t)p.S * p.K * (2 * p.dp + 4));
   w.ln_part = c.take<double>(kRefineBlocks);
-  w.L = c.take<float>((size_t)p.N * p.Kp);
+  w.L = c.take<float>((size_t)npad_of(p.N) * p.Kp);  // Lt [Kp][Npad]
   w.bytes = c.bytes();
   return w;
 }
@@ -997,7 +1029,7 @@ int tc_launch(const TcPlan &p, const float *X, const float *pts, const TcWs &w, 
   }
   tc_pass1_kernel<NKC><<<p.grid1, kThreads, smem1_bytes(), st>>>(
       m_phi, m_plo, m_qhi, m_qlo, w.cst2, p.N, p.n_pt, p.n_ct, p.G, p.tpg, w.part_m, w.part_s,
-      w.part_tv, w.part_ti, w.L, p.Kp);
+      w.part_tv, w.part_ti, w.L, npad_of(p.N));
   FGMM_LAUNCH_CHECK("tc_pass1_kernel");
   mark(st, "tc_pass1_kernel");
   {
@@ -1009,11 +1041,11 @@ int tc_launch(const TcPlan &p, const float *X, const float *pts, const TcWs &w, 
     if (vec && (D) % 4 == 0 && 8 * (D) == p.d)                                                  \
       tc_refine_kernel<D, true><<<blocks, 256, 0, st>>>(X, p.N, p.d, w.sc, w.ms, w.lc, w.part_m, \
                                                         w.part_s, w.part_tv, w.part_ti, p.G,     \
-                                                        w.ln2x, w.L, p.Kp, ln, w.ln_part);       \
+                                                        w.ln2x, w.L, npad_of(p.N), ln, w.ln_part); \
     else                                                                                        \
       tc_refine_kernel<D, false><<<blocks, 256, 0, st>>>(X, p.N, p.d, w.sc, w.ms, w.lc,          \
                                                          w.part_m, w.part_s, w.part_tv,          \
-                                                         w.part_ti, p.G, w.ln2x, w.L, p.Kp, ln,  \
+                                                         w.part_ti, p.G, w.ln2x, w.L, npad_of(p.N), ln, \
                                                          w.ln_part);                             \
   } while (0)
     if (dpl <= 1) FGMM_REFINE(1);
@@ -1029,7 +1061,7 @@ int tc_launch(const TcPlan &p, const float *X, const float *pts, const TcWs &w, 
   CUtensorMap m_fhi, m_flo, m_l;
   if ((rc = make_map_atoms(&m_fhi, phi, rows, p.KA, kSlicePts))) return rc;
   if ((rc = make_map_atoms(&m_flo, plo, rows, p.KA, kSlicePts))) return rc;
-  if ((rc = make_map(&m_l, w.L, p.N, p.Kp, kSlicePts, CU_TENSOR_MAP_SWIZZLE_NONE, NC))) return rc;
+  if ((rc = make_map(&m_l, w.L, p.Kp, (int)npad_of(p.N), NC, CU_TENSOR_MAP_SWIZZLE_64B, kSlicePts))) return rc;
   tc_stats_kernel<NKC><<<p.grid2, kThreads2, smem2_bytes(NKC * KC), st>>>(
       m_fhi, m_flo, m_l, w.ln2x, p.N, p.S, p.K, w.partial);
   FGMM_LAUNCH_CHECK("tc_stats_kernel");
@@ -1081,6 +1113,12 @@ int tc_em_stats(const float *X, const void *points, int64_t N, int d, const floa
                          st);
 }
 
+#ifdef FGMM_EXP_TIMING1
+extern "C" int fgmm_exp_timing1(unsigned long long *out, int n) {
+  cudaDeviceSynchronize();
+  return (int)cudaMemcpyFromSymbol(out, g_tim1, sizeof(unsigned long long) * 8 * n);
+}
+#endif
 #ifdef FGMM_EXP_TIMING
 extern "C" int fgmm_exp_timing(unsigned long long *out, int n) {
   cudaDeviceSynchronize();
