@@ -45,10 +45,11 @@ namespace {
 constexpr int BM = 128;                       // points per tile
 constexpr int NC = 128;                       // components per tile
 constexpr int KC = 32;                        // fp32 elements per K chunk (one 128-byte row)
-constexpr int kEpiWarps = 8;                  // two warps per TMEM lane quarter
+constexpr int kEpiWarps = 16;                 // four warps per TMEM lane quarter
 constexpr int kThreads = 64 + 32 * kEpiWarps; // warp 0 TMA, warp 1 MMA, warps 2.. epilogue
 constexpr int kEpiThreads = 32 * kEpiWarps;
-constexpr int kHalf = 64;                     // columns of a tile owned by one epilogue warp
+constexpr int kPart = 32;                     // columns of a tile owned by one epilogue warp
+constexpr int kParts = NC / kPart;            // epilogue warps per lane quarter
 constexpr int kStages1 = 3;
 constexpr int kTileBytes = BM * KC * 4;       // 16 KB: 128 rows x 128 B
 constexpr int kStageBytes = 4 * kTileBytes;   // 64 KB
@@ -204,22 +205,20 @@ __device__ __forceinline__ bool issue_dist_chunk(uint32_t base, uint32_t tmem, u
   return true;
 }
 
-// Epilogue side: add the next group buffer into acc (this warp's 32 rows, its 64 columns;
-// lane_tmem already points at the warp's lane quarter and column half).
+// Epilogue side: add the next group buffer into acc (this warp's 32 rows, its 32 columns;
+// lane_tmem already points at the warp's lane quarter and column part).
 template <int NB, bool kFirst>
 __device__ __forceinline__ bool drain_group(uint32_t lane_tmem, uint32_t &gcount, uint32_t tfull0,
-                                            uint32_t tempty0, float (&acc)[kHalf], int lane) {
+                                            uint32_t tempty0, float (&acc)[kPart], int lane) {
   const uint32_t buf = gcount % NB, use = gcount / NB;
   if (!__all_sync(0xffffffffu, mbar_wait(tfull0 + 8u * buf, use & 1u, kErrWaitTmemFull)))
     return false;
   tc_fence_after();
-  float v[kHalf];  // all loads in flight before the one wait
-#pragma unroll
-  for (int h = 0; h < kHalf / 32; ++h)
-    tmem_ld32(lane_tmem + buf * NC + h * 32, *reinterpret_cast<float(*)[32]>(v + h * 32));
+  float v[kPart];
+  tmem_ld32(lane_tmem + buf * NC, v);
   tmem_wait_ld();
 #pragma unroll
-  for (int e = 0; e < kHalf; ++e) acc[e] = kFirst ? v[e] : acc[e] + v[e];
+  for (int e = 0; e < kPart; ++e) acc[e] = kFirst ? v[e] : acc[e] + v[e];
   tc_fence_before();
   __syncwarp();
   if (lane == 0) mbar_arrive(tempty0 + 8u * buf);
@@ -249,8 +248,8 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * kStageBytes);
   // bars: full[S] empty[S] tfull[NB] tempty[NB] done
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 2 * NB + 1);
-  struct Half { float m, s, v1, v2; int i1, i2; };
-  Half *lse_x = reinterpret_cast<Half *>(tmem_slot + 2);  // [128] half-row exchange
+  struct Part { float m, s, v1, v2; int i1, i2; };
+  Part *lse_x = reinterpret_cast<Part *>(tmem_slot + 2);  // [kParts - 1][128] row exchange
   const uint32_t bar0 = smem_u32(bars);
   auto FULL = [&](int s) { return bar0 + 8u * s; };
   auto EMPTY = [&](int s) { return bar0 + 8u * (S + s); };
@@ -338,9 +337,9 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
     }
     __syncwarp();
   } else {
-    const int q = warp & 3, half = (warp - 2) >> 2;
+    const int q = warp & 3, part = (warp - 2) >> 2;
     const int row = q * 32 + lane;
-    const uint32_t lane_tmem = tmem + ((uint32_t)(q * 32) << 16) + half * kHalf;
+    const uint32_t lane_tmem = tmem + ((uint32_t)(q * 32) << 16) + part * kPart;
     uint32_t gcount = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
@@ -351,7 +350,7 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
       int i1 = -1, i2 = -1;
       const int64_t n_row = (int64_t)pt * BM + row;
       for (int t = g * tpg; t < t1 && ok; ++t) {
-        float acc[kHalf];
+        float acc[kPart];
         T1TICK(D1);
         ok = drain_group<NB, true>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
         T1TICK(C1);
@@ -360,59 +359,68 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
           ok = drain_group<NB, false>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
         T1TICK(A1);
         if (!ok) break;
-        const float *cp = cst2 + (int64_t)t * NC + half * kHalf;
+        const int kb = t * NC + part * kPart;
+        float cst[kPart];
 #pragma unroll
-        for (int j = 0; j < kHalf / 32; ++j) {
-          float cm = -INFINITY;
+        for (int e = 0; e < kPart; ++e) cst[e] = __ldg(cst2 + kb + e);
+        float c4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            acc[j * 32 + e] = fmaf(acc[j * 32 + e], -0.5f * kLog2e, __ldg(cp + j * 32 + e));
-            cm = fmaxf(cm, acc[j * 32 + e]);
-          }
-          {  // the log2-likelihood matrix feeds the statistics pass; stored transposed
-             // (Lt [component][point]) so that each store of a warp is 32 consecutive points
-            float *lp = Lt + (int64_t)(t * NC + half * kHalf + j * 32) * Npad + n_row;
+        for (int e = 0; e < kPart; ++e) {
+          acc[e] = fmaf(acc[e], -0.5f * kLog2e, cst[e]);
+          c4[e & 3] = fmaxf(c4[e & 3], acc[e]);
+        }
+        const float cm = fmaxf(fmaxf(c4[0], c4[1]), fmaxf(c4[2], c4[3]));
+        {  // the log2-likelihood matrix feeds the statistics pass; stored transposed
+           // (Lt [component][point]) so that each store of a warp is 32 consecutive points
+          float *lp = Lt + (int64_t)kb * Npad + n_row;
 #pragma unroll
-            for (int e = 0; e < 32; ++e) lp[(int64_t)e * Npad] = acc[j * 32 + e];
-          }
-          const float mn = fmaxf(m, cm);
-          const float mr = (mn == -INFINITY) ? 0.0f : mn;
-          float a = s * ex2(m - mr);
+          for (int e = 0; e < kPart; ++e) lp[(int64_t)e * Npad] = acc[e];
+        }
+        const float mn = fmaxf(m, cm);
+        const float mr = (mn == -INFINITY) ? 0.0f : mn;
+        float a4[4] = {s * ex2(m - mr), 0.0f, 0.0f, 0.0f};
 #pragma unroll
-          for (int e = 0; e < 32; ++e) a += ex2(acc[j * 32 + e] - mr);
-          s = a;
-          m = mn;
-          if (cm > v2) {  // rare once the row's leading components are known
-            const int kb = t * NC + half * kHalf + j * 32;
+        for (int e = 0; e < kPart; ++e) a4[e & 3] += ex2(acc[e] - mr);
+        s = (a4[0] + a4[1]) + (a4[2] + a4[3]);
+        m = mn;
+        if (cm > v2) {  // rare once the row's leading components are known
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const float x = acc[j * 32 + e];
-              if (x > v2) {
-                if (x > v1) { v2 = v1; i2 = i1; v1 = x; i1 = kb + e; }
-                else        { v2 = x; i2 = kb + e; }
-              }
+          for (int e = 0; e < kPart; ++e) {
+            const float x = acc[e];
+            if (x > v2) {
+              if (x > v1) { v2 = v1; i2 = i1; v1 = x; i1 = kb + e; }
+              else        { v2 = x; i2 = kb + e; }
             }
           }
         }
       }
       T1TICK(B1);
-      // merge the two column halves of each row
-      if (half == 1) lse_x[row] = Half{m, s, v1, v2, i1, i2};
+      // merge the column parts of each row
+      if (part > 0) lse_x[(part - 1) * BM + row] = Part{m, s, v1, v2, i1, i2};
       ok = epi_sync_and(ok);
-      if (half == 0) {
-        const Half o = lse_x[row];
-        const float mn = fmaxf(m, o.m);
+      if (part == 0) {
+        Part o[kParts];
+        o[0] = Part{m, s, v1, v2, i1, i2};
+#pragma unroll
+        for (int r = 1; r < kParts; ++r) o[r] = lse_x[(r - 1) * BM + row];
+        float mn = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < kParts; ++r) mn = fmaxf(mn, o[r].m);
         const float mr = (mn == -INFINITY) ? 0.0f : mn;
-        const float sm = s * ex2(m - mr) + o.s * ex2(o.m - mr);
-        float c[4] = {v1, v2, o.v1, o.v2};
-        int ci[4] = {i1, i2, o.i1, o.i2};
+        float sm = 0.0f;
         float b1 = -INFINITY, b2 = -INFINITY;
         int j1 = -1, j2 = -1;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          if (c[e] > b2) {
-            if (c[e] > b1) { b2 = b1; j2 = j1; b1 = c[e]; j1 = ci[e]; }
-            else           { b2 = c[e]; j2 = ci[e]; }
+        for (int r = 0; r < kParts; ++r) {
+          sm += o[r].s * ex2(o[r].m - mr);
+          const float c[2] = {o[r].v1, o[r].v2};
+          const int ci[2] = {o[r].i1, o[r].i2};
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            if (c[e] > b2) {
+              if (c[e] > b1) { b2 = b1; j2 = j1; b1 = c[e]; j1 = ci[e]; }
+              else           { b2 = c[e]; j2 = ci[e]; }
+            }
           }
         }
         const int64_t n = (int64_t)pt * BM + row;
@@ -998,7 +1006,7 @@ TcWs tc_layout(void *ws, const TcPlan &p) {
   return w;
 }
 
-size_t smem1_bytes() { return 1024 + kStages1 * kStageBytes + 256 + 128 * 24; }
+size_t smem1_bytes() { return 1024 + kStages1 * kStageBytes + 256 + (kParts - 1) * BM * 24; }
 size_t smem2_bytes(int KA) {
   switch (KA) {
     case 64: return StatsShape<64>::kSmem;
