@@ -242,13 +242,14 @@ def run_reference(args, wl):
 
 # ------------------------------------------------------------------------ our arm
 def profile_dominant(C, X, points, mu, var, lp, ws, reps=5):
-    """CUDA-event duration of every launch of one em_stats call (avg over reps)."""
+    """CUDA-event durations of the launches of one em_stats call, summed per kernel name
+    (a kernel runs once per point chunk), averaged over `reps` calls: ms per iteration."""
     import ctypes
     from flashgmm_b200 import _lib
     lib = _lib.load()
     N, d = X.shape
     K = mu.shape[0]
-    nmax = 16
+    nmax = 128
     acc = {}
     for _ in range(reps):
         ms = (ctypes.c_float * nmax)()
@@ -261,8 +262,8 @@ def profile_dominant(C, X, points, mu, var, lp, ws, reps=5):
         for i in range(nmax):
             if names[i] is None:
                 break
-            acc.setdefault(names[i].decode(), []).append(ms[i])
-    return {k: sum(v) / len(v) for k, v in acc.items()}
+            acc[names[i].decode()] = acc.get(names[i].decode(), 0.0) + ms[i]
+    return {k: v / reps for k, v in acc.items()}
 
 
 def run_ours(args, wl):

@@ -49,7 +49,7 @@ int num_sms();
 
 // Optional per-launch event recording (active only inside fgmm_em_stats_profiled).
 struct PhaseTimer {
-  static constexpr int kMax = 16;
+  static constexpr int kMax = 128;
   cudaEvent_t ev[kMax + 1];
   const char *name[kMax];
   int n = 0;

@@ -282,6 +282,8 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
   if (warp == 0) {
     if (lane == 0) {
       prefetch_tmap(&tm_phi); prefetch_tmap(&tm_plo); prefetch_tmap(&tm_qhi); prefetch_tmap(&tm_qlo);
+      // the points stream through once per component group; the parameters are re-read
+      const uint64_t pol_p = policy_evict_first(), pol_q = policy_evict_last();
       int stage = 0;
       uint32_t phase = 0, armed = 0, armed_par = 0;
       bool ok = true;
@@ -295,10 +297,10 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
             T1TICK(A1);
             const uint32_t base = smem_u32(smem + stage * kStageBytes);
             mbar_arrive_expect_tx(FULL(stage), kStageBytes);
-            tma_load_2d(base, &tm_phi, c * KC, pt * BM, FULL(stage));
-            tma_load_2d(base + kTileBytes, &tm_plo, c * KC, pt * BM, FULL(stage));
-            tma_load_2d(base + 2 * kTileBytes, &tm_qhi, c * KC, t * NC, FULL(stage));
-            tma_load_2d(base + 3 * kTileBytes, &tm_qlo, c * KC, t * NC, FULL(stage));
+            tma_load_2d_hint(base, &tm_phi, c * KC, pt * BM, FULL(stage), pol_p);
+            tma_load_2d_hint(base + kTileBytes, &tm_plo, c * KC, pt * BM, FULL(stage), pol_p);
+            tma_load_2d_hint(base + 2 * kTileBytes, &tm_qhi, c * KC, t * NC, FULL(stage), pol_q);
+            tma_load_2d_hint(base + 3 * kTileBytes, &tm_qlo, c * KC, t * NC, FULL(stage), pol_q);
             armed |= 1u << stage;
             armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
             if (++stage == S) { stage = 0; phase ^= 1; }
@@ -339,6 +341,7 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
   } else {
     const int q = warp & 3, part = (warp - 2) >> 2;
     const int row = q * 32 + lane;
+    const uint64_t pol_l = policy_evict_last();
     const uint32_t lane_tmem = tmem + ((uint32_t)(q * 32) << 16) + part * kPart;
     uint32_t gcount = 0;
     bool ok = true;
@@ -372,9 +375,10 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
         const float cm = fmaxf(fmaxf(c4[0], c4[1]), fmaxf(c4[2], c4[3]));
         {  // the log2-likelihood matrix feeds the statistics pass; stored transposed
            // (Lt [component][point]) so that each store of a warp is 32 consecutive points
+          // kept in L2 for the statistics pass (evict_last)
           float *lp = Lt + (int64_t)kb * Npad + n_row;
 #pragma unroll
-          for (int e = 0; e < kPart; ++e) lp[(int64_t)e * Npad] = acc[e];
+          for (int e = 0; e < kPart; ++e) st_hint(lp + (int64_t)e * Npad, acc[e], pol_l);
         }
         const float mn = fmaxf(m, cm);
         const float mr = (mn == -INFINITY) ? 0.0f : mn;
@@ -468,7 +472,7 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
                  const float *__restrict__ part_m, const float *__restrict__ part_s,
                  const float2 *__restrict__ part_tv, const int2 *__restrict__ part_ti, int G,
                  float *__restrict__ ln2x, float *__restrict__ Lt, int64_t Npad,
-                 float *__restrict__ ln_out, double *__restrict__ ln_part) {
+                 float *__restrict__ ln_out, double *__restrict__ ln_part, int acc_ln) {
   __shared__ double wsum[8];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int sub = lane & 7;           // lane within the point's group of 8
@@ -574,7 +578,7 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
   if (threadIdx.x == 0) {
     double t = 0.0;
     for (int w = 0; w < 8; ++w) t += wsum[w];
-    ln_part[blockIdx.x] = t;
+    ln_part[blockIdx.x] = acc_ln ? ln_part[blockIdx.x] + t : t;  // chunks add up in order
   }
 }
 
@@ -633,7 +637,7 @@ template <int NKC>
 __global__ void __launch_bounds__(kThreads2, 1)
 tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constant__ CUtensorMap tm_flo,
                 const __grid_constant__ CUtensorMap tm_l, const float *__restrict__ ln2x, int64_t N,
-                int S_slots, int K, float *__restrict__ partial) {
+                int S_slots, int K, float *__restrict__ partial, int accum) {
   constexpr int KA = NKC * KC;
   constexpr int DP = KA / 2;
   constexpr int PSTRIDE = 2 * DP + 4;
@@ -838,6 +842,8 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
       prefetch_tmap(&tm_flo);
       prefetch_tmap(&tm_l);
     }
+    // L is read exactly once
+    const uint64_t pol_l = policy_evict_first();
     for (int s = 0; s < S && ok; ++s) {
       // same rule as the gamma warps, NST slices ahead (before the EMPTY wait below)
       while (nf < T && s >= kSlicesFlush * (nf + 1) + NST && ok) flush_next(false);
@@ -853,7 +859,7 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
         mbar_arrive_expect_tx(FULL(st), 2 * Sh::kFPart + kSlicePts * NC * 4 + kSlicePts * 4);
         tma_load_3d(base, &tm_fhi, 0, (int32_t)nb, 0, FULL(st));
         tma_load_3d(base + Sh::kFPart, &tm_flo, 0, (int32_t)nb, 0, FULL(st));
-        tma_load_2d(base + Sh::kLOff, &tm_l, (int32_t)nb, ct * NC, FULL(st));
+        tma_load_2d_hint(base + Sh::kLOff, &tm_l, (int32_t)nb, ct * NC, FULL(st), pol_l);
         bulk_load(base + Sh::kNOff, ln2x + nb, kSlicePts * 4, FULL(st));
       }
       __syncwarp();
@@ -874,17 +880,25 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
 #pragma unroll
     for (int e = 0; e < SEG; e += 4) {
       const int f = seg * SEG + e;  // feature column: x^2 part first, then x
-      float *o = dst + (f < DP ? DP + f : f - DP);
-      *reinterpret_cast<float4 *>(o) = ok ? make_float4(sacc[e], sacc[e + 1], sacc[e + 2], sacc[e + 3])
-                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 *o = reinterpret_cast<float4 *>(dst + (f < DP ? DP + f : f - DP));
+      float4 v = ok ? make_float4(sacc[e], sacc[e + 1], sacc[e + 2], sacc[e + 3])
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (accum) {  // a later chunk of the same iteration: this CTA slot's row adds up
+        const float4 o0 = *o;
+        v = make_float4(o0.x + v.x, o0.y + v.y, o0.z + v.z, o0.w + v.w);
+      }
+      *o = v;
     }
   }
   // n_k: the two gamma warps of a lane quarter add up their halves of the points
   float *nk_s = reinterpret_cast<float *>(smem);  // [128], the stage ring is idle now
   if (warp >= 4 && warp < kGammaWarps) nk_s[cl] = nk;
   __syncthreads();
-  if (warp < 4 && k < K)
-    partial[((int64_t)slot * K + k) * PSTRIDE + 2 * DP] = ok ? nk + nk_s[cl] : 0.0f;
+  if (warp < 4 && k < K) {
+    float *o = partial + ((int64_t)slot * K + k) * PSTRIDE + 2 * DP;
+    const float v = ok ? nk + nk_s[cl] : 0.0f;
+    *o = accum ? *o + v : v;
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -946,10 +960,41 @@ int make_map(CUtensorMap *m, const float *base, int64_t rows, int cols, int box_
   return FGMM_OK;
 }
 
-struct TcPlan {
-  int64_t N;
-  int d, dp, KA, nkc, K, Kp, n_ct, n_pt, G, tpg, S, grid1, grid2;
+// The points are processed in chunks whose log2-likelihood block Lt [Kp][chunk] fits a
+// fixed budget well inside the 126 MB L2: pass 1 writes it, the refine kernel patches it
+// and the statistics kernel reads it back while it is still cache-resident, and the
+// workspace stays bounded for any N.  Chunks run in order on the stream; the per-slot
+// statistics rows and the log-normalizer block sums add up across chunks.
+#ifndef FGMM_L_CHUNK_MB
+#define FGMM_L_CHUNK_MB 64
+#endif
+constexpr int64_t kLChunkBytes = (int64_t)FGMM_L_CHUNK_MB << 20;
+
+// Launch geometry of one chunk of Nc points.
+struct TcChunk {
+  int64_t Nc;
+  int n_pt, G, tpg, S, grid1, grid2;
 };
+
+struct TcPlan {
+  int64_t N, Nc;  // all points; points per chunk (a multiple of 128, the last may be short)
+  int d, dp, KA, nkc, K, Kp, n_ct, chunks;
+  TcChunk first;
+};
+
+TcChunk chunk_plan(int64_t Nc, int n_ct) {
+  TcChunk c{};
+  c.Nc = Nc;
+  c.n_pt = (int)cdiv(Nc, BM);
+  const int sms = num_sms();
+  const int G = (int)std::min<int64_t>(n_ct, std::max<int64_t>(1, cdiv(4 * sms, c.n_pt)));
+  c.tpg = (int)cdiv(n_ct, G);
+  c.G = (int)cdiv(n_ct, c.tpg);
+  c.grid1 = (int)std::min<int64_t>((int64_t)c.n_pt * c.G, sms);
+  c.S = (int)std::max<int64_t>(1, std::min<int64_t>(sms / std::max(1, n_ct), cdiv(Nc, 32)));
+  c.grid2 = n_ct * c.S;
+  return c;
+}
 
 TcPlan plan(int64_t N, int d, int K) {
   TcPlan p{};
@@ -959,18 +1004,10 @@ TcPlan plan(int64_t N, int d, int K) {
   p.nkc = p.KA / KC;
   p.n_ct = (int)cdiv(K, NC);
   p.Kp = p.n_ct * NC;
-  p.n_pt = (int)cdiv(N, BM);
-  const int sms = num_sms();
-#ifndef FGMM_G_OVERRIDE
-  int G = (int)std::min<int64_t>(p.n_ct, std::max<int64_t>(1, cdiv(4 * sms, p.n_pt)));
-#else
-  int G = (int)std::min<int64_t>(p.n_ct, std::max<int64_t>(1, cdiv(FGMM_G_OVERRIDE * sms, p.n_pt)));
-#endif
-  p.tpg = (int)cdiv(p.n_ct, G);
-  p.G = (int)cdiv(p.n_ct, p.tpg);
-  p.grid1 = (int)std::min<int64_t>((int64_t)p.n_pt * p.G, sms);
-  p.S = (int)std::max<int64_t>(1, std::min<int64_t>(sms / std::max(1, p.n_ct), cdiv(N, 32)));
-  p.grid2 = p.n_ct * p.S;
+  const int64_t fit = std::max<int64_t>(BM, kLChunkBytes / ((int64_t)p.Kp * 4) / BM * BM);
+  p.Nc = std::min<int64_t>(npad_of(N), fit);
+  p.chunks = (int)cdiv(N, p.Nc);
+  p.first = chunk_plan(std::min<int64_t>(N, p.Nc), p.n_ct);
   return p;
 }
 
@@ -985,23 +1022,26 @@ struct TcWs {
 constexpr int kRefineBlocks = 8192;  // 32 points per block
 inline int refine_blocks(int64_t N) { return (int)std::min<int64_t>(kRefineBlocks, cdiv(N, 32)); }
 
+// Per-chunk buffers are sized for the first (largest) chunk; the component-group
+// partials for n_ct groups, the most any chunk uses.
 TcWs tc_layout(void *ws, const TcPlan &p) {
   TcWs w{};
   Carve c(ws);
+  const int64_t Nc = p.first.Nc;
   w.qhi = c.take<float>((size_t)p.Kp * p.KA);
   w.qlo = c.take<float>((size_t)p.Kp * p.KA);
   w.cst2 = c.take<float>(p.Kp);
   w.sc = c.take<float>((size_t)p.K * p.d);
   w.ms = c.take<float>((size_t)p.K * p.d);
   w.lc = c.take<float>(p.K);
-  w.part_m = c.take<float>((size_t)p.G * p.N);
-  w.part_s = c.take<float>((size_t)p.G * p.N);
-  w.part_tv = c.take<float2>((size_t)p.G * p.N);
-  w.part_ti = c.take<int2>((size_t)p.G * p.N);
-  w.ln2x = c.take<float>(p.N);
-  w.partial = c.take<float>((size_t)p.S * p.K * (2 * p.dp + 4));
+  w.part_m = c.take<float>((size_t)p.n_ct * Nc);
+  w.part_s = c.take<float>((size_t)p.n_ct * Nc);
+  w.part_tv = c.take<float2>((size_t)p.n_ct * Nc);
+  w.part_ti = c.take<int2>((size_t)p.n_ct * Nc);
+  w.ln2x = c.take<float>(npad_of(Nc));
+  w.partial = c.take<float>((size_t)p.first.S * p.K * (2 * p.dp + 4));
   w.ln_part = c.take<double>(kRefineBlocks);
-  w.L = c.take<float>((size_t)npad_of(p.N) * p.Kp);  // Lt [Kp][Npad]
+  w.L = c.take<float>((size_t)npad_of(Nc) * p.Kp);  // Lt [Kp][chunk]
   w.bytes = c.bytes();
   return w;
 }
@@ -1015,46 +1055,44 @@ size_t smem2_bytes(int KA) {
     default: return StatsShape<256>::kSmem;
   }
 }
+
+// Pass 1, refine and statistics for the chunk of points [n0, n0 + c.Nc).
 template <int NKC>
-int tc_launch(const TcPlan &p, const float *X, const float *pts, const TcWs &w, float *ln,
-              cudaStream_t st) {
-  const float *phi = pts;
-  const float *plo = pts + points_half_floats(p.N, p.d);
-  const int64_t rows = npad_of(p.N);
+int tc_launch_chunk(const TcPlan &p, const TcChunk &c, int64_t n0, bool first, const float *X,
+                    const float *pts, const TcWs &w, float *ln, cudaStream_t st) {
+  const float *phi = pts + n0 * p.KA;
+  const float *plo = pts + points_half_floats(p.N, p.d) + n0 * p.KA;
+  const int64_t rows = npad_of(c.Nc);
+  const int64_t lcols = npad_of(c.Nc);
+  const float *Xc = X + n0 * p.d;
   CUtensorMap m_phi, m_plo, m_qhi, m_qlo;
   int rc;
   if ((rc = make_map(&m_phi, phi, rows, p.KA, BM))) return rc;
   if ((rc = make_map(&m_plo, plo, rows, p.KA, BM))) return rc;
   if ((rc = make_map(&m_qhi, w.qhi, p.Kp, p.KA, NC))) return rc;
   if ((rc = make_map(&m_qlo, w.qlo, p.Kp, p.KA, NC))) return rc;
-  static bool attr_done[5] = {};
-  if (!attr_done[NKC / 2]) {
-    FGMM_CUDA_TRY(cudaFuncSetAttribute(tc_pass1_kernel<NKC>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1_bytes()));
-    FGMM_CUDA_TRY(cudaFuncSetAttribute(tc_stats_kernel<NKC>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2_bytes(NKC * KC)));
-    attr_done[NKC / 2] = true;
-  }
-  tc_pass1_kernel<NKC><<<p.grid1, kThreads, smem1_bytes(), st>>>(
-      m_phi, m_plo, m_qhi, m_qlo, w.cst2, p.N, p.n_pt, p.n_ct, p.G, p.tpg, w.part_m, w.part_s,
-      w.part_tv, w.part_ti, w.L, npad_of(p.N));
+  tc_pass1_kernel<NKC><<<c.grid1, kThreads, smem1_bytes(), st>>>(
+      m_phi, m_plo, m_qhi, m_qlo, w.cst2, c.Nc, c.n_pt, p.n_ct, c.G, c.tpg, w.part_m, w.part_s,
+      w.part_tv, w.part_ti, w.L, lcols);
   FGMM_LAUNCH_CHECK("tc_pass1_kernel");
   mark(st, "tc_pass1_kernel");
   {
-    const int blocks = refine_blocks(p.N);
+    const int blocks = refine_blocks(c.Nc);
     const int dpl = (p.d + 7) / 8;
-    const bool vec = p.d % 32 == 0 && reinterpret_cast<uintptr_t>(X) % 16 == 0;  // d = 8 DPL
-#define FGMM_REFINE(D)                                                                          \
-  do {                                                                                          \
-    if (vec && (D) % 4 == 0 && 8 * (D) == p.d)                                                  \
-      tc_refine_kernel<D, true><<<blocks, 256, 0, st>>>(X, p.N, p.d, w.sc, w.ms, w.lc, w.part_m, \
-                                                        w.part_s, w.part_tv, w.part_ti, p.G,     \
-                                                        w.ln2x, w.L, npad_of(p.N), ln, w.ln_part); \
-    else                                                                                        \
-      tc_refine_kernel<D, false><<<blocks, 256, 0, st>>>(X, p.N, p.d, w.sc, w.ms, w.lc,          \
-                                                         w.part_m, w.part_s, w.part_tv,          \
-                                                         w.part_ti, p.G, w.ln2x, w.L, npad_of(p.N), ln, \
-                                                         w.ln_part);                             \
+    const bool vec = p.d % 32 == 0 && reinterpret_cast<uintptr_t>(Xc) % 16 == 0;  // d = 8 DPL
+    const int acc = first ? 0 : 1;
+#define FGMM_REFINE(D)                                                                             \
+  do {                                                                                             \
+    if (vec && (D) % 4 == 0 && 8 * (D) == p.d)                                                     \
+      tc_refine_kernel<D, true><<<blocks, 256, 0, st>>>(Xc, c.Nc, p.d, w.sc, w.ms, w.lc, w.part_m, \
+                                                        w.part_s, w.part_tv, w.part_ti, c.G,       \
+                                                        w.ln2x, w.L, lcols, ln + n0, w.ln_part,    \
+                                                        acc);                                      \
+    else                                                                                           \
+      tc_refine_kernel<D, false><<<blocks, 256, 0, st>>>(Xc, c.Nc, p.d, w.sc, w.ms, w.lc,          \
+                                                         w.part_m, w.part_s, w.part_tv,            \
+                                                         w.part_ti, c.G, w.ln2x, w.L, lcols,       \
+                                                         ln + n0, w.ln_part, acc);                 \
   } while (0)
     if (dpl <= 1) FGMM_REFINE(1);
     else if (dpl <= 2) FGMM_REFINE(2);
@@ -1069,17 +1107,38 @@ int tc_launch(const TcPlan &p, const float *X, const float *pts, const TcWs &w, 
   CUtensorMap m_fhi, m_flo, m_l;
   if ((rc = make_map_atoms(&m_fhi, phi, rows, p.KA, kSlicePts))) return rc;
   if ((rc = make_map_atoms(&m_flo, plo, rows, p.KA, kSlicePts))) return rc;
-  if ((rc = make_map(&m_l, w.L, p.Kp, (int)npad_of(p.N), NC, CU_TENSOR_MAP_SWIZZLE_64B, kSlicePts))) return rc;
-  tc_stats_kernel<NKC><<<p.grid2, kThreads2, smem2_bytes(NKC * KC), st>>>(
-      m_fhi, m_flo, m_l, w.ln2x, p.N, p.S, p.K, w.partial);
+  if ((rc = make_map(&m_l, w.L, p.Kp, (int)lcols, NC, CU_TENSOR_MAP_SWIZZLE_64B, kSlicePts))) return rc;
+  tc_stats_kernel<NKC><<<c.grid2, kThreads2, smem2_bytes(NKC * KC), st>>>(
+      m_fhi, m_flo, m_l, w.ln2x, c.Nc, c.S, p.K, w.partial, first ? 0 : 1);
   FGMM_LAUNCH_CHECK("tc_stats_kernel");
   mark(st, "tc_stats_kernel");
   return FGMM_OK;
 }
 
+template <int NKC>
+int tc_launch(const TcPlan &p, const float *X, const float *pts, const TcWs &w, float *ln,
+              cudaStream_t st) {
+  static bool attr_done[5] = {};
+  if (!attr_done[NKC / 2]) {
+    FGMM_CUDA_TRY(cudaFuncSetAttribute(tc_pass1_kernel<NKC>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1_bytes()));
+    FGMM_CUDA_TRY(cudaFuncSetAttribute(tc_stats_kernel<NKC>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2_bytes(NKC * KC)));
+    attr_done[NKC / 2] = true;
+  }
+  for (int i = 0; i < p.chunks; ++i) {
+    const int64_t n0 = (int64_t)i * p.Nc;
+    const int64_t nc = std::min<int64_t>(p.Nc, p.N - n0);
+    const TcChunk c = nc == p.first.Nc ? p.first : chunk_plan(nc, p.n_ct);
+    const int rc = tc_launch_chunk<NKC>(p, c, n0, i == 0, X, pts, w, ln, st);
+    if (rc) return rc;
+  }
+  return FGMM_OK;
+}
+
 }  // namespace
 
-int tc_launches(int64_t, int, int) { return 5; }
+int tc_launches(int64_t N, int d, int K) { return 2 + 3 * plan(N, d, K).chunks; }
 
 bool tc_supported(int64_t N, int d, int K) { return N >= 1 && K >= 1 && d >= 1 && d <= kMaxDp; }
 
@@ -1117,8 +1176,8 @@ int tc_em_stats(const float *X, const void *points, int64_t N, int d, const floa
     default: return fail(FGMM_ERR_UNSUPPORTED, "tcgen05 family: d > 128");
   }
   if (rc) return rc;
-  return reduce_partials(w.partial, p.S, K, d, p.dp, 2 * p.dp + 4, w.ln_part, refine_blocks(N), stats,
-                         st);
+  return reduce_partials(w.partial, p.first.S, K, d, p.dp, 2 * p.dp + 4, w.ln_part,
+                         refine_blocks(p.first.Nc), stats, st);
 }
 
 #ifdef FGMM_EXP_TIMING1

@@ -108,7 +108,7 @@ int fgmm_em_stats_launches(int64_t N, int32_t d, int32_t K);
 /* Profiling variant of fgmm_em_stats: identical launches, with a CUDA event
  * recorded on `stream` before the first and after every launch.  Synchronises
  * the stream, then writes the duration (ms) of each launch into
- * launch_ms[0 .. min(n, launches)-1] and, if names != NULL, a static name
+ * launch_ms[0 .. min(n, launches, 128)-1] and, if names != NULL, a static name
  * string per launch.  Returns the status of the wrapped call.  Has no
  * counterpart in the reference (its launcher exposes no timing). */
 int fgmm_em_stats_profiled(const float *X, const void *points, int64_t N, int32_t d,

@@ -177,6 +177,25 @@ def test_tail_and_padding_sizes(family):
         check(f"N={N} K={K} d={d}", got, g, SLACK_BY_FAMILY[family])
 
 
+def test_point_chunks(family):
+    """A K large enough that the tensor-core family splits the points into several chunks
+    (its log-likelihood block is bounded); the statistics and log-normalizer sums across
+    chunks must match the reference's fp32 algorithm like any single-chunk case."""
+    from flashgmm_b200 import flash_gmm_native as C, _lib
+    from flashgmm_b200.data import make_mixture, init_params
+    dev = torch.device("cuda:0")
+    N, K, d = 20000, 1100, 32
+    if family == "tc":
+        assert _lib.load().fgmm_em_stats_launches(N, d, K) >= 2 + 3 * 2, "expected >= 2 chunks"
+    X, *_ = make_mixture(N, K, d, seed=11)
+    mu, var, lp = init_params(X, K, seed=4)
+    got = [o.cpu().numpy() for o in C.flash_em_fused(X.to(dev), mu.to(dev), var.to(dev), lp.to(dev))]
+    g = {"X": X.numpy(), "mu": mu.numpy(), "var": var.numpy(), "log_pi": lp.numpy()}
+    ref = oracle.flash_em_fused(X, mu, var, lp, BK=8, nthreads=8)
+    g.update(new_mu=ref[0], new_var=ref[1], new_log_pi=ref[2], log_normalizer=ref[3])
+    check(f"N={N} K={K} d={d}", got, g, SLACK_BY_FAMILY[family])
+
+
 def test_sharded_class_single_rank_matches_native():
     """DistributedFlashGMM on one NCCL rank == NativeFlashGMM (same kernels, one no-op
     all_reduce per iteration)."""
