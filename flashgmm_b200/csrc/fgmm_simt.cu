@@ -146,7 +146,7 @@ simt_pass1_kernel(const float *__restrict__ X, int64_t N, int d, const float *__
 
 // grid: (slots, cdiv(K, kTK)).  Block (s, ct) accumulates components
 // [ct*kTK, ct*kTK + kTK) over points [s*chunk, (s+1)*chunk) and writes
-// partial[s][k][0..2d] = [s_k | sq_k | n_k].
+// partial[k][s][0..2d] = [s_k | sq_k | n_k].
 template <int DPL>
 __global__ void __launch_bounds__(kThreads)
 simt_pass2_kernel(const float *__restrict__ X, int64_t N, int d, const float *__restrict__ sc,
@@ -215,8 +215,10 @@ simt_pass2_kernel(const float *__restrict__ X, int64_t N, int d, const float *__
     }
     __syncthreads();
   }
-  float *dst = partial + ((int64_t)blockIdx.x * K + k0) * W;
-  for (int i = threadIdx.x; i < tk * W; i += kThreads) dst[i] = acc_sm[i];
+  for (int kk = 0; kk < tk; ++kk) {  // partial[k][slot][0..2d]
+    float *dst = partial + ((int64_t)(k0 + kk) * gridDim.x + blockIdx.x) * W;
+    for (int i = threadIdx.x; i < W; i += kThreads) dst[i] = acc_sm[kk * W + i];
+  }
 }
 
 struct SimtWs {

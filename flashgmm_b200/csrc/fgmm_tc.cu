@@ -631,8 +631,8 @@ __device__ __forceinline__ bool cta_sync_and(bool v) {
 #ifdef FGMM_EXP_TIMING
 __device__ unsigned long long g_tim[2048][8];
 #endif
-// Partial statistics row (per CTA slot and component): [s (DP) | sq (DP) | n | pad],
-// stride 2 DP + 4.
+// Partial statistics row (per component and CTA slot, partial[k][slot]):
+// [s (DP) | sq (DP) | n | pad], stride 2 DP + 4.
 template <int NKC>
 __global__ void __launch_bounds__(kThreads2, 1)
 tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constant__ CUtensorMap tm_flo,
@@ -876,7 +876,7 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
   ok = cta_sync_and(ok);
   const int k = ct * NC + cl;
   if (k < K) {
-    float *dst = partial + ((int64_t)slot * K + k) * PSTRIDE;
+    float *dst = partial + ((int64_t)k * S_slots + slot) * PSTRIDE;
 #pragma unroll
     for (int e = 0; e < SEG; e += 4) {
       const int f = seg * SEG + e;  // feature column: x^2 part first, then x
@@ -895,7 +895,7 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
   if (warp >= 4 && warp < kGammaWarps) nk_s[cl] = nk;
   __syncthreads();
   if (warp < 4 && k < K) {
-    float *o = partial + ((int64_t)slot * K + k) * PSTRIDE + 2 * DP;
+    float *o = partial + ((int64_t)k * S_slots + slot) * PSTRIDE + 2 * DP;
     const float v = ok ? nk + nk_s[cl] : 0.0f;
     *o = accum ? *o + v : v;
   }

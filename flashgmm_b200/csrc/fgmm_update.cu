@@ -8,7 +8,8 @@
 
 namespace fgmm {
 
-// partials: [slots][K][W] fp32, each row laid out [s (ds) | sq (ds) | n | ...] where only
+// partials: [K][slots][W] fp32 (a component's rows contiguous), each row laid out
+// [s (ds) | sq (ds) | n | ...] where only
 // the first d of each ds-wide run are meaningful; stats: [n (K) | s (K d) | sq (K d) | sum ln].
 // A block takes 32 consecutive output values (lane = value, so the loads of a warp are
 // contiguous) and splits the slots over its 8 warps (warp g sums slots g, g + 8, ... with
@@ -16,29 +17,29 @@ namespace fgmm {
 // so the result does not depend on timing.  Block 0 also sums the per-block
 // log-normalizer partials into the last entry.
 constexpr int kRedGroups = 8;
-constexpr int kRedUnroll = 16;  // loads in flight per thread (one round trip up to 128 slots)
-__global__ void __launch_bounds__(32 * kRedGroups)
+constexpr int kRedUnroll = 10;  // loads in flight per thread (one round trip up to 80 slots)
+__global__ void __launch_bounds__(32 * kRedGroups, 6)  // six blocks (1536 threads) per SM
 reduce_partials_kernel(const float *__restrict__ part, int slots, int K, int d, int ds, int W,
                        const double *__restrict__ lnp, int ln_slots, double *__restrict__ stats) {
   __shared__ double sh[kRedGroups][32];
   const int V = 2 * d + 1;
   const int64_t total = (int64_t)K * V;
-  const int64_t slot_stride = (int64_t)K * W;
+  const int64_t slot_stride = W;
   const int lane = threadIdx.x & 31, g = threadIdx.x >> 5;
   for (int64_t base = (int64_t)blockIdx.x * 32; base < total; base += (int64_t)gridDim.x * 32) {
     const int64_t i = base + lane;
     const bool live = i < total;
     const int k = live ? (int)(i / V) : 0, c = live ? (int)(i % V) : 0;
     const int src = c < d ? c : (c < 2 * d ? ds + (c - d) : 2 * ds);
-    const float *p = part + (int64_t)k * W + src;
+    const float *p = part + (int64_t)k * slots * W + src;
     double acc = 0.0;
-    for (int s = g; s < slots; s += kRedUnroll * kRedGroups) {  // all loads, then the adds
+    const int n_mine = live && g < slots ? (slots - g + kRedGroups - 1) / kRedGroups : 0;
+    const float *q = p + (int64_t)g * slot_stride;
+    const int step = kRedGroups * (int)slot_stride;
+    for (int s = 0; s < n_mine; s += kRedUnroll) {  // all loads of a batch, then the adds
       float v[kRedUnroll];
 #pragma unroll
-      for (int u = 0; u < kRedUnroll; ++u) {
-        const int ss = s + u * kRedGroups;
-        v[u] = (live && ss < slots) ? __ldg(p + (int64_t)ss * slot_stride) : 0.0f;
-      }
+      for (int u = 0; u < kRedUnroll; ++u) v[u] = s + u < n_mine ? __ldg(q + (s + u) * step) : 0.0f;
 #pragma unroll
       for (int u = 0; u < kRedUnroll; ++u) acc += (double)v[u];
     }
@@ -72,7 +73,10 @@ reduce_partials_kernel(const float *__restrict__ part, int slots, int K, int d, 
 int reduce_partials(const float *partials, int slots, int K, int d, int ds, int W,
                     const double *ln_partials, int ln_slots, double *stats, cudaStream_t stream) {
   const int64_t total = (int64_t)K * (2 * d + 1);
-  int blocks = (int)std::min<int64_t>(cdiv(total, 32), 16 * num_sms());
+#ifndef FGMM_RED_BLOCKS_PER_SM
+#define FGMM_RED_BLOCKS_PER_SM 16
+#endif
+  int blocks = (int)std::min<int64_t>(cdiv(total, 32), FGMM_RED_BLOCKS_PER_SM * num_sms());
   reduce_partials_kernel<<<blocks, 32 * kRedGroups, 0, stream>>>(partials, slots, K, d, ds, W,
                                                                  ln_partials, ln_slots, stats);
   FGMM_LAUNCH_CHECK("reduce_partials_kernel");
