@@ -38,6 +38,10 @@ SIGNATURES = {
     "fgmm_em_fused_workspace_bytes": (_sz, [_i64, _i32, _i32]),
     "fgmm_em_fused_static": (ctypes.c_int, [_vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp]),
     "fgmm_em_fused": (ctypes.c_int, [_vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "fgmm_e_step_workspace_bytes": (ctypes.c_size_t, [_i64, _i32, _i32]),
+    "fgmm_e_step": (ctypes.c_int, [_vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _sz, _vp]),
+    "fgmm_m_step_workspace_bytes": (ctypes.c_size_t, [_i64, _i32, _i32]),
+    "fgmm_m_step": (ctypes.c_int, [_vp, _i64, _i32, _vp, _i32, _vp, _vp, _vp, _vp, _sz, _vp]),
 }
 
 _lib = None

@@ -167,6 +167,48 @@ int fgmm_em_fused(const float *X, int64_t N, int32_t d, const float *mu, const f
   return fgmm_em_update(stats, (double)N, K, d, new_mu, new_var, new_log_pi, stream);
 }
 
+size_t fgmm_e_step_workspace_bytes(int64_t N, int32_t d, int32_t K) {
+  if (N < 1 || K < 1 || d < 1 || d > 256) return 0;
+  return estep_workspace_bytes(N, d, K);
+}
+
+int fgmm_e_step(const float *X, int64_t N, int32_t d, const float *mu, const float *var,
+                const float *log_pi, int32_t K, float *gamma, float *log_normalizer,
+                void *workspace, size_t workspace_bytes, void *stream) {
+  int rc = check_shape(N, d, K);
+  if (rc) return rc;
+  if (!X || !mu || !var || !log_pi || !gamma || !log_normalizer || !workspace)
+    return fail(FGMM_ERR_INVALID, "null pointer argument");
+  if (!aligned(workspace, 256)) return fail(FGMM_ERR_INVALID, "workspace must be 256-byte aligned");
+  if (workspace_bytes < estep_workspace_bytes(N, d, K))
+    return fail(FGMM_ERR_WORKSPACE, "workspace too small");
+  return estep(X, N, d, mu, var, log_pi, K, gamma, log_normalizer, workspace, (cudaStream_t)stream);
+}
+
+size_t fgmm_m_step_workspace_bytes(int64_t N, int32_t d, int32_t K) {
+  if (N < 1 || K < 1 || d < 1 || d > 256) return 0;
+  return align_up(mstep_workspace_bytes(N, d, K), 256) +
+         align_up((size_t)fgmm_stats_len(K, d) * sizeof(double), 256);
+}
+
+int fgmm_m_step(const float *X, int64_t N, int32_t d, const float *gamma, int32_t K,
+                float *new_mu, float *new_var, float *new_log_pi, void *workspace,
+                size_t workspace_bytes, void *stream) {
+  int rc = check_shape(N, d, K);
+  if (rc) return rc;
+  if (!X || !gamma || !new_mu || !new_var || !new_log_pi || !workspace)
+    return fail(FGMM_ERR_INVALID, "null pointer argument");
+  if (!aligned(workspace, 256)) return fail(FGMM_ERR_INVALID, "workspace must be 256-byte aligned");
+  const size_t need = fgmm_m_step_workspace_bytes(N, d, K);
+  if (workspace_bytes < need) return fail(FGMM_ERR_WORKSPACE, "workspace too small");
+  const size_t stats_off = align_up(mstep_workspace_bytes(N, d, K), 256);
+  double *stats = reinterpret_cast<double *>(static_cast<char *>(workspace) + stats_off);
+  cudaStream_t st = (cudaStream_t)stream;
+  rc = mstep_stats(X, N, d, gamma, K, stats, workspace, st);
+  if (rc) return rc;
+  return em_update(stats, (double)N, K, d, new_mu, new_var, new_log_pi, st, /*floors=*/false);
+}
+
 int fgmm_device_error(int reset) { return tc_device_error(reset != 0); }
 
 int fgmm_em_stats_launches(int64_t N, int32_t d, int32_t K) {

@@ -90,6 +90,21 @@ int reduce_partials(const float *partials, int slots, int K, int d, int ds, int 
                     const double *ln_partials, int ln_slots, double *stats,
                     cudaStream_t stream);
 int em_update(const double *stats, double n_total, int K, int d, float *new_mu,
-              float *new_var, float *new_log_pi, cudaStream_t stream);
+              float *new_var, float *new_log_pi, cudaStream_t stream, bool floors = true);
+
+// Direct-form parameters: sc = var^-1/2, ms = mu var^-1/2 ([K][d]) and
+// lc = log_pi - 1/2 (d log 2pi + sum log var) ([K]) (fgmm_simt.cu).
+int prep_direct_params(const float *mu, const float *var, const float *log_pi, int K, int d,
+                       float *sc, float *ms, float *lc, cudaStream_t stream);
+
+// ---- E-step / M-step with materialised responsibilities (fgmm_estep.cu, fgmm_simt.cu) ----
+size_t estep_workspace_bytes(int64_t N, int d, int K);
+int estep(const float *X, int64_t N, int d, const float *mu, const float *var,
+          const float *log_pi, int K, float *gamma, float *log_norm, void *ws,
+          cudaStream_t stream);
+size_t mstep_workspace_bytes(int64_t N, int d, int K);
+// Packed fp64 statistics [n | s | sq | 0] of given responsibilities gamma[N][K].
+int mstep_stats(const float *X, int64_t N, int d, const float *gamma, int K, double *stats,
+                void *ws, cudaStream_t stream);
 
 }  // namespace fgmm

@@ -147,11 +147,14 @@ simt_pass1_kernel(const float *__restrict__ X, int64_t N, int d, const float *__
 // grid: (slots, cdiv(K, kTK)).  Block (s, ct) accumulates components
 // [ct*kTK, ct*kTK + kTK) over points [s*chunk, (s+1)*chunk) and writes
 // partial[k][s][0..2d] = [s_k | sq_k | n_k].
-template <int DPL>
+// GIN: the responsibilities are given (gamma[N][K], the standard M-step) instead of
+// being recomputed from the parameters and the log-normalizer.
+template <int DPL, bool GIN>
 __global__ void __launch_bounds__(kThreads)
 simt_pass2_kernel(const float *__restrict__ X, int64_t N, int d, const float *__restrict__ sc,
                   const float *__restrict__ ms, const float *__restrict__ lc, int K,
-                  const float *__restrict__ ln, int64_t chunk, float *__restrict__ partial) {
+                  const float *__restrict__ ln, int64_t chunk, float *__restrict__ partial,
+                  const float *__restrict__ gamma) {
   extern __shared__ float sm[];
   float *s_t = sm;                   // [kTK][d]
   float *m_t = s_t + kTK * d;        // [kTK][d]
@@ -161,11 +164,13 @@ simt_pass2_kernel(const float *__restrict__ X, int64_t N, int d, const float *__
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int k0 = blockIdx.y * kTK;
   const int tk = min(kTK, K - k0);
-  for (int i = threadIdx.x; i < tk * d; i += kThreads) {
-    s_t[i] = sc[(int64_t)k0 * d + i];
-    m_t[i] = ms[(int64_t)k0 * d + i];
+  if (!GIN) {
+    for (int i = threadIdx.x; i < tk * d; i += kThreads) {
+      s_t[i] = sc[(int64_t)k0 * d + i];
+      m_t[i] = ms[(int64_t)k0 * d + i];
+    }
+    if (threadIdx.x < tk) c_t[threadIdx.x] = lc[k0 + threadIdx.x];
   }
-  if (threadIdx.x < tk) c_t[threadIdx.x] = lc[k0 + threadIdx.x];
   for (int i = threadIdx.x; i < kTK * W; i += kThreads) acc_sm[i] = 0.0f;
   __syncthreads();
 
@@ -181,12 +186,17 @@ simt_pass2_kernel(const float *__restrict__ X, int64_t N, int d, const float *__
   for (int64_t n = pbeg + warp; n < pend; n += kWarps) {
     float x[DPL];
     load_x<DPL>(X, n, d, lane, x);
-    const float l = __ldg(ln + n);
+    const float l = GIN ? 0.0f : __ldg(ln + n);
 #pragma unroll
     for (int kk = 0; kk < kTK; ++kk) {
       if (kk < tk) {
-        const float ll = c_t[kk] - 0.5f * mahal<DPL>(x, s_t + kk * d, m_t + kk * d, d, lane);
-        const float g = expf(ll - l);
+        float g;
+        if (GIN) {
+          g = __ldg(gamma + n * K + k0 + kk);
+        } else {
+          const float ll = c_t[kk] - 0.5f * mahal<DPL>(x, s_t + kk * d, m_t + kk * d, d, lane);
+          g = expf(ll - l);
+        }
         an[kk] += g;
 #pragma unroll
         for (int i = 0; i < DPL; ++i) {
@@ -258,17 +268,57 @@ int simt_launch(const float *X, int64_t N, int d, int K, const SimtWs &w, float 
   mark(st, "simt_pass1_kernel");
   const size_t sm2 = (size_t)(2 * kTK * d + kTK + kTK * (2 * d + 1)) * sizeof(float);
   if (sm2 > 48 * 1024)
-    FGMM_CUDA_TRY(cudaFuncSetAttribute(simt_pass2_kernel<DPL>,
+    FGMM_CUDA_TRY(cudaFuncSetAttribute(simt_pass2_kernel<DPL, false>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2));
   dim3 grid(w.slots, (unsigned)cdiv(K, kTK));
-  simt_pass2_kernel<DPL><<<grid, kThreads, sm2, st>>>(X, N, d, w.sc, w.ms, w.lc, K, ln, w.chunk,
-                                                      w.partial);
+  simt_pass2_kernel<DPL, false><<<grid, kThreads, sm2, st>>>(X, N, d, w.sc, w.ms, w.lc, K, ln,
+                                                             w.chunk, w.partial, nullptr);
   FGMM_LAUNCH_CHECK("simt_pass2_kernel");
   mark(st, "simt_pass2_kernel");
   return FGMM_OK;
 }
 
+template <int DPL>
+int mstep_launch(const float *X, int64_t N, int d, const float *gamma, int K, const SimtWs &w,
+                 cudaStream_t st) {
+  const size_t sm2 = (size_t)(2 * kTK * d + kTK + kTK * (2 * d + 1)) * sizeof(float);
+  if (sm2 > 48 * 1024)
+    FGMM_CUDA_TRY(cudaFuncSetAttribute(simt_pass2_kernel<DPL, true>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2));
+  dim3 grid(w.slots, (unsigned)cdiv(K, kTK));
+  simt_pass2_kernel<DPL, true><<<grid, kThreads, sm2, st>>>(X, N, d, nullptr, nullptr, nullptr, K,
+                                                            nullptr, w.chunk, w.partial, gamma);
+  FGMM_LAUNCH_CHECK("simt_mstep_kernel");
+  return FGMM_OK;
+}
+
 }  // namespace
+
+int prep_direct_params(const float *mu, const float *var, const float *log_pi, int K, int d,
+                       float *sc, float *ms, float *lc, cudaStream_t st) {
+  simt_prep_kernel<<<K, 64, 0, st>>>(mu, var, log_pi, K, d, sc, ms, lc);
+  FGMM_LAUNCH_CHECK("simt_prep_kernel");
+  return FGMM_OK;
+}
+
+size_t mstep_workspace_bytes(int64_t N, int d, int K) { return simt_layout(nullptr, N, d, K).bytes; }
+
+int mstep_stats(const float *X, int64_t N, int d, const float *gamma, int K, double *stats,
+                void *ws, cudaStream_t st) {
+  SimtWs w = simt_layout(ws, N, d, K);
+  const int dpl = (d + 31) / 32;
+  int rc;
+  switch (dpl) {
+    case 1: rc = mstep_launch<1>(X, N, d, gamma, K, w, st); break;
+    case 2: rc = mstep_launch<2>(X, N, d, gamma, K, w, st); break;
+    case 3: rc = mstep_launch<3>(X, N, d, gamma, K, w, st); break;
+    case 4: rc = mstep_launch<4>(X, N, d, gamma, K, w, st); break;
+    case 5: case 6: rc = mstep_launch<6>(X, N, d, gamma, K, w, st); break;
+    default: rc = mstep_launch<8>(X, N, d, gamma, K, w, st); break;
+  }
+  if (rc != FGMM_OK) return rc;
+  return reduce_partials(w.partial, w.slots, K, d, d, 2 * d + 1, w.ln_part, 0, stats, st);
+}
 
 int simt_launches() { return 4; }
 

@@ -84,26 +84,33 @@ int reduce_partials(const float *partials, int slots, int K, int d, int ds, int 
   return FGMM_OK;
 }
 
+// floors = 1: the fused path's update (flash_gmm_cpu.cpp:270-284): n_k and the weight
+// floored at 1e-8.  floors = 0: the reference's standard M-step
+// (flash_gmm/csrc/binding.cpp:82-90, flash_gmm_cpu.cpp:292-311): plain division by n_k and
+// log(n_k / N), only the variance clamped (a NaN stays NaN, as torch's clamp_min keeps it).
 __global__ void em_update_kernel(const double *__restrict__ stats, double n_total, int K, int d,
                                  float *__restrict__ new_mu, float *__restrict__ new_var,
-                                 float *__restrict__ new_log_pi) {
+                                 float *__restrict__ new_log_pi, int floors) {
   const int k = blockIdx.x;
   const double nk = stats[k];
-  const double inv = 1.0 / fmax(nk, 1e-8);
+  const double inv = 1.0 / (floors ? fmax(nk, 1e-8) : nk);
   const double *s = stats + K + (int64_t)k * d;
   const double *q = stats + K + (int64_t)K * d + (int64_t)k * d;
   for (int j = threadIdx.x; j < d; j += blockDim.x) {
     const double m = s[j] * inv;
+    const double v = q[j] * inv - m * m;
     new_mu[(int64_t)k * d + j] = (float)m;
-    new_var[(int64_t)k * d + j] = (float)fmax(q[j] * inv - m * m, 1e-6);
+    new_var[(int64_t)k * d + j] = (float)(v < 1e-6 ? 1e-6 : v);
   }
-  if (threadIdx.x == 0) new_log_pi[k] = (float)log(fmax(nk / n_total, 1e-8));
+  if (threadIdx.x == 0)
+    new_log_pi[k] = (float)(floors ? log(fmax(nk / n_total, 1e-8)) : log(nk / n_total));
 }
 
 int em_update(const double *stats, double n_total, int K, int d, float *new_mu, float *new_var,
-              float *new_log_pi, cudaStream_t stream) {
+              float *new_log_pi, cudaStream_t stream, bool floors) {
   int threads = d >= 128 ? 128 : (d >= 64 ? 64 : 32);
-  em_update_kernel<<<K, threads, 0, stream>>>(stats, n_total, K, d, new_mu, new_var, new_log_pi);
+  em_update_kernel<<<K, threads, 0, stream>>>(stats, n_total, K, d, new_mu, new_var, new_log_pi,
+                                              floors ? 1 : 0);
   FGMM_LAUNCH_CHECK("em_update_kernel");
   return FGMM_OK;
 }

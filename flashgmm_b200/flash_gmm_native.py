@@ -21,8 +21,8 @@ import torch
 
 from . import _lib
 
-__all__ = ["flash_em_fused", "em_stats", "em_update", "prepare_points", "stats_len",
-           "family_for", "set_family"]
+__all__ = ["flash_em_fused", "standard_e_step", "flash_e_step", "standard_m_step", "em_stats",
+           "em_update", "prepare_points", "stats_len", "family_for", "set_family"]
 
 
 def _stream_ptr(device):
@@ -95,6 +95,69 @@ def flash_em_fused(X, mu, var, log_pi, BN=64, BK=8):
                                      new_lp.data_ptr(), ln.data_ptr(), ws.data_ptr(), ws.numel(),
                                      _stream_ptr(dev)))
     return [new_mu, new_var, new_lp, ln]
+
+
+def standard_e_step(X, mu, var, log_pi):
+    """E-step with materialised responsibilities -> ``[gamma[N, K], log_normalizer[N]]``.
+
+    Same contract as the reference op (``flash_gmm/csrc/binding.cpp:35-49``, CUDA kernels
+    ``flash_gmm/csrc/flash_gmm_cuda.cu:328-400``).
+    """
+    X, mu, var, log_pi, N, d, K = _check_params(X, mu, var, log_pi)
+    lib = _lib.load()
+    dev = X.device
+    with torch.cuda.device(dev):
+        nb = lib.fgmm_e_step_workspace_bytes(N, d, K)
+        if nb == 0:
+            raise RuntimeError(f"standard_e_step: unsupported shape N={N} K={K} d={d}")
+        ws = _workspace(nb, dev)
+        gamma = torch.empty(N, K, dtype=torch.float32, device=dev)
+        ln = torch.empty(N, dtype=torch.float32, device=dev)
+        _lib.check(lib.fgmm_e_step(X.data_ptr(), N, d, mu.data_ptr(), var.data_ptr(),
+                                   log_pi.data_ptr(), K, gamma.data_ptr(), ln.data_ptr(),
+                                   ws.data_ptr(), ws.numel(), _stream_ptr(dev)))
+    return [gamma, ln]
+
+
+def flash_e_step(X, mu, var, log_pi, BK=4):
+    """Same outputs as :func:`standard_e_step` (``flash_gmm/csrc/binding.cpp:51-60``).
+
+    The reference runs this op on the CPU only and refuses CUDA tensors; here it runs on
+    the GPU.  ``BK`` (the reference's component tile of its online log-sum-exp) is
+    accepted and ignored: the result does not depend on it.
+    """
+    return standard_e_step(X, mu, var, log_pi)
+
+
+def standard_m_step(X, gamma):
+    """M-step from responsibilities -> ``[new_mu, new_var, new_log_pi]``.
+
+    Same contract and formulas as the reference op (``flash_gmm/csrc/binding.cpp:78-92``):
+    no floor on ``n_k``, variance clamped at 1e-6, ``log_pi = log(n_k / N)``; the sums are
+    accumulated in fp64.
+    """
+    _check_f32_cuda("X", X, 2)
+    dev = X.device
+    _check_f32_cuda("gamma", gamma, 2, dev)
+    X = X.contiguous()
+    gamma = gamma.contiguous()
+    N, d = X.shape
+    if gamma.shape[0] != N:
+        raise RuntimeError(f"shape mismatch: X{tuple(X.shape)} gamma{tuple(gamma.shape)}")
+    K = gamma.shape[1]
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        nb = lib.fgmm_m_step_workspace_bytes(N, d, K)
+        if nb == 0:
+            raise RuntimeError(f"standard_m_step: unsupported shape N={N} K={K} d={d}")
+        ws = _workspace(nb, dev)
+        out = [torch.empty(K, d, dtype=torch.float32, device=dev),
+               torch.empty(K, d, dtype=torch.float32, device=dev),
+               torch.empty(K, dtype=torch.float32, device=dev)]
+        _lib.check(lib.fgmm_m_step(X.data_ptr(), N, d, gamma.data_ptr(), K, out[0].data_ptr(),
+                                   out[1].data_ptr(), out[2].data_ptr(), ws.data_ptr(),
+                                   ws.numel(), _stream_ptr(dev)))
+    return out
 
 
 def prepare_points(X, K):

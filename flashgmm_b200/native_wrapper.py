@@ -1,4 +1,5 @@
-"""Drop-in for the reference's ``flash_gmm/native_wrapper.py`` model classes.
+"""Drop-in for the reference's ``flash_gmm/native_wrapper.py`` model classes
+(``NativeFlashGMM`` and ``NativeStandardGMM``).
 
 ``NativeFlashGMM(K, d, BN=64, BK=8, max_iter=100, tol=1e-4, seed=42).fit(X)``
 keeps the reference's constructor, attributes (``mu``, ``var``, ``log_pi``),
@@ -19,22 +20,10 @@ import torch
 from . import flash_gmm_native as _C
 
 
-class NativeFlashGMM:
-    """Flash-GMM EM on B200 kernels (no N x K matrix is ever materialised)."""
-
-    def __init__(self, K: int, d: int, BN: int = 64, BK: int = 8,
-                 max_iter: int = 100, tol: float = 1e-4, seed: int = 42, device=None):
-        self.K = K
-        self.d = d
-        self.BN = BN
-        self.BK = BK
-        self.max_iter = max_iter
-        self.tol = tol
-        self.seed = seed
-        self.device = device
-        self.mu = None
-        self.var = None
-        self.log_pi = None
+class _EMModel:
+    """What both model classes share: the reference's initialisation
+    (``flash_gmm/native_wrapper.py:64-70, 115-121``), moving X to the GPU, and
+    ``predict_proba`` / ``predict`` (``flash_gmm/flash_gmm.py:185-193``)."""
 
     def _init_params(self, X: torch.Tensor):
         N = X.shape[0]
@@ -52,6 +41,79 @@ class NativeFlashGMM:
         if X.is_pinned():
             return X.to(dev, non_blocking=True)
         return X.to(dev)
+
+    def predict_proba(self, X: torch.Tensor) -> torch.Tensor:
+        """Responsibilities gamma[N, K] under the fitted parameters (the E-step op)."""
+        X = self._to_device(X).contiguous()
+        gamma, _ = _C.flash_e_step(X, self.mu, self.var, self.log_pi)
+        return gamma
+
+    def predict(self, X: torch.Tensor) -> torch.Tensor:
+        return self.predict_proba(X).argmax(dim=1)
+
+
+class NativeStandardGMM(_EMModel):
+    """Standard EM (materialised L and gamma) on this package's CUDA kernels.
+
+    Drop-in for ``NativeStandardGMM`` (``flash_gmm/native_wrapper.py:48-96``): same
+    constructor, initialisation, history and stopping rule; each iteration is
+    ``standard_e_step`` then ``standard_m_step``.
+    """
+
+    def __init__(self, K: int, d: int, max_iter: int = 100, tol: float = 1e-4, seed: int = 42,
+                 device=None):
+        self.K = K
+        self.d = d
+        self.max_iter = max_iter
+        self.tol = tol
+        self.seed = seed
+        self.device = device
+        self.mu = None
+        self.var = None
+        self.log_pi = None
+
+    def fit(self, X: torch.Tensor, verbose: bool = False, init=None):
+        """Run EM; ``init=(mu, var, log_pi)`` overrides the random initialisation."""
+        X = self._to_device(X).contiguous()
+        if init is not None:
+            self.mu, self.var, self.log_pi = (t.to(X.device).contiguous() for t in init)
+        else:
+            self._init_params(X)
+        prev_ll = -float("inf")
+        history = []
+        for it in range(self.max_iter):
+            t0 = time.time()
+            gamma, log_norm = _C.standard_e_step(X, self.mu, self.var, self.log_pi)
+            avg_ll = log_norm.mean().item()
+            self.mu, self.var, self.log_pi = _C.standard_m_step(X, gamma)
+            elapsed = time.time() - t0
+            history.append({"iter": it, "log_likelihood": avg_ll, "time_ms": elapsed * 1000})
+            if verbose and (it % 10 == 0 or it < 5):
+                print(f"  iter {it:3d}: LL={avg_ll:.4f}  time={elapsed*1000:.1f}ms")
+            if abs(avg_ll - prev_ll) < self.tol:
+                if verbose:
+                    print(f"  Converged at iter {it}")
+                break
+            prev_ll = avg_ll
+        return history
+
+
+class NativeFlashGMM(_EMModel):
+    """Flash-GMM EM on B200 kernels (no N x K matrix is ever materialised)."""
+
+    def __init__(self, K: int, d: int, BN: int = 64, BK: int = 8,
+                 max_iter: int = 100, tol: float = 1e-4, seed: int = 42, device=None):
+        self.K = K
+        self.d = d
+        self.BN = BN
+        self.BK = BK
+        self.max_iter = max_iter
+        self.tol = tol
+        self.seed = seed
+        self.device = device
+        self.mu = None
+        self.var = None
+        self.log_pi = None
 
     def fit(self, X: torch.Tensor, verbose: bool = False, init=None):
         """Run EM; ``init=(mu, var, log_pi)`` overrides the random initialisation."""

@@ -94,6 +94,28 @@ int fgmm_em_fused(const float *X, int64_t N, int32_t d,
                   float *new_mu, float *new_var, float *new_log_pi, float *log_normalizer,
                   void *workspace, size_t workspace_bytes, void *stream);
 
+/* E-step with materialised responsibilities: gamma[N][K] (row-major) and
+ * log_normalizer[N], the log-likelihood in the reference's direct form.  The
+ * drop-in for the ops `standard_e_step(X, mu, var, log_pi)` and
+ * `flash_e_step(X, mu, var, log_pi, BK)` (flash_gmm/csrc/binding.cpp:35-60;
+ * CUDA standard_e_step_cuda, flash_gmm/csrc/flash_gmm_cuda.cu:328-400; the
+ * reference runs flash_e_step on the CPU only, flash_gmm_cpu.cpp:108-168). */
+size_t fgmm_e_step_workspace_bytes(int64_t N, int32_t d, int32_t K);
+int fgmm_e_step(const float *X, int64_t N, int32_t d,
+                const float *mu, const float *var, const float *log_pi, int32_t K,
+                float *gamma, float *log_normalizer,
+                void *workspace, size_t workspace_bytes, void *stream);
+
+/* M-step from given responsibilities gamma[N][K]: the drop-in for the op
+ * `standard_m_step(X, gamma)` (flash_gmm/csrc/binding.cpp:78-92; CPU
+ * flash_gmm_cpu.cpp:292-311): mu = gamma^T X / n_k, var = max(gamma^T X^2 / n_k
+ * - mu^2, 1e-6), log_pi = log(n_k / N), n_k = sum_n gamma[n][k], with no floor on
+ * n_k (as in the reference).  Statistics are summed in fp64. */
+size_t fgmm_m_step_workspace_bytes(int64_t N, int32_t d, int32_t K);
+int fgmm_m_step(const float *X, int64_t N, int32_t d, const float *gamma, int32_t K,
+                float *new_mu, float *new_var, float *new_log_pi,
+                void *workspace, size_t workspace_bytes, void *stream);
+
 /* Synchronises the device and returns the code of the first failure a
  * tensor-core kernel recorded (0 = none): every wait inside those kernels is
  * bounded, and a wait that runs out records its code here and makes the kernel

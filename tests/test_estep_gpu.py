@@ -1,0 +1,144 @@
+"""The materialised-responsibility ops: ``standard_e_step`` / ``flash_e_step`` /
+``standard_m_step`` (reference ``flash_gmm/csrc/binding.cpp:35-60, 78-92``), the
+``NativeStandardGMM`` model and ``predict_proba`` / ``predict``.
+
+Responsibilities and log-normalizers are compared like the fused iteration: both ours
+and the reference's own fp32 outputs (golden fixture from its compiled CPU op, or the
+bit-exact C restatement for larger shapes) are measured against an fp64 evaluation of
+the same formulas, and ours must be within ``SLACK`` of the reference's own error (plus
+a small absolute floor); the log-normalizer must also meet the north star's 1e-3
+absolute.  The M-step is compared with the fp64 evaluation of the reference's formulas
+at 1e-4 (scale-aware, as in ``tests/helpers.py``).
+"""
+import numpy as np
+import pytest
+import torch
+
+from helpers import load_golden
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda:0")
+SLACK = 2.0
+
+
+def estep_f64(X, mu, var, lp):
+    """gamma, ln in fp64 (direct-form log-likelihood, expanded with fp64 matmuls)."""
+    X, mu, var, lp = (np.asarray(a, np.float64) for a in (X, mu, var, lp))
+    d = X.shape[1]
+    iv = 1.0 / var
+    maha = (X * X) @ iv.T - 2.0 * X @ (mu * iv).T + np.sum(mu * mu * iv, 1)[None, :]
+    L = lp[None, :] - 0.5 * (d * np.log(2 * np.pi) + np.sum(np.log(var), 1)[None, :] + maha)
+    m = L.max(1, keepdims=True)
+    ln = (m + np.log(np.exp(L - m).sum(1, keepdims=True)))[:, 0]
+    return np.exp(L - ln[:, None]), ln
+
+
+def check_estep(got_g, got_ln, ref_g, ref_ln, X, mu, var, lp):
+    g64, ln64 = estep_f64(X, mu, var, lp)
+    eg, rg = np.max(np.abs(got_g - g64)), np.max(np.abs(ref_g - g64))
+    el, rl = np.max(np.abs(got_ln - ln64)), np.max(np.abs(ref_ln - ln64))
+    assert eg <= SLACK * rg + 1e-6, (eg, rg)
+    assert el <= SLACK * rl + 1e-5, (el, rl)
+    # rows sum to one as well as the reference's own rows do
+    es, rs = np.max(np.abs(got_g.sum(1) - 1.0)), np.max(np.abs(ref_g.sum(1) - 1.0))
+    assert es <= SLACK * rs + 1e-5, (es, rs)
+
+
+def _t(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+def test_e_step_golden():
+    from flashgmm_b200 import flash_gmm_native as C
+    g = load_golden("estep_c1_1024")
+    args = [_t(g[k]) for k in ("X", "mu", "var", "log_pi")]
+    P = [g[k] for k in ("X", "mu", "var", "log_pi")]
+    gam, ln = [o.cpu().numpy() for o in C.standard_e_step(*args)]
+    check_estep(gam, ln, g["gamma"], g["log_normalizer"], *P)
+    fg, fln = [o.cpu().numpy() for o in C.flash_e_step(*args, BK=4)]
+    check_estep(fg, fln, g["flash_gamma"], g["flash_log_normalizer"], *P)
+
+
+def test_m_step_golden():
+    from flashgmm_b200 import flash_gmm_native as C
+    g = load_golden("estep_c1_1024")
+    mu, var, lp = [o.cpu().numpy() for o in C.standard_m_step(_t(g["X"]), _t(g["gamma"]))]
+    scale = np.maximum(np.abs(g["m_mu"]), np.sqrt(g["m_var"]))
+    assert np.max(np.abs(mu - g["m_mu"]) / scale) < 1e-4
+    assert np.max(np.abs(var - g["m_var"]) / g["m_var"]) < 1e-4
+    assert np.max(np.abs(lp - g["m_log_pi"])) < 1e-4
+
+
+@pytest.mark.parametrize("N,K,d", [(5000, 300, 100), (3000, 37, 200), (257, 513, 1), (1, 1, 3)])
+def test_e_and_m_step_vs_reference_algorithm(N, K, d):
+    from flashgmm_b200 import flash_gmm_native as C
+    from flashgmm_b200.data import make_mixture, init_params
+    X, *_ = make_mixture(N, K, d, seed=N + K + d)
+    if K <= N:
+        mu, var, lp = init_params(X, K, seed=2)
+    else:
+        mu = torch.randn(K, d, generator=torch.Generator().manual_seed(3)) * 2
+        var = torch.ones(K, d)
+        lp = torch.full((K,), -float(np.log(K)))
+    var = var * (0.5 + torch.rand(K, d, generator=torch.Generator().manual_seed(4)))
+    gam, ln = [o.cpu().numpy() for o in C.standard_e_step(_t(X), _t(mu), _t(var), _t(lp))]
+    P = [X.numpy(), mu.numpy(), var.numpy(), lp.numpy()]
+    rg, rln = oracle.standard_e_step(*P, nthreads=8)
+    check_estep(gam, ln, rg, rln, *P)
+    # M-step from the reference's own responsibilities, against the fp64 evaluation of
+    # the reference's formulas (binding.cpp:82-90)
+    G = rg.astype(np.float64)
+    Xd = X.numpy().astype(np.float64)
+    nk = G.sum(0)
+    rmu = (G.T @ Xd) / nk[:, None]
+    rvar = np.maximum((G.T @ (Xd * Xd)) / nk[:, None] - rmu ** 2, 1e-6)
+    rlp = np.log(nk / N)
+    mu2, var2, lp2 = [o.cpu().numpy() for o in C.standard_m_step(_t(X), _t(rg))]
+    keep = nk / N > 1e-4
+    scale = np.maximum(np.abs(rmu), np.sqrt(rvar))
+    assert np.max((np.abs(mu2 - rmu) / scale)[keep], initial=0) < 1e-4
+    assert np.max((np.abs(var2 - rvar) / (rmu ** 2 + rvar))[keep], initial=0) < 1e-5
+    assert np.max(np.abs(lp2 - rlp)[keep], initial=0) < 1e-4
+
+
+def test_m_step_empty_component_matches_reference_semantics():
+    """The reference's standard M-step has no floor on n_k: an empty component gives a
+    NaN mean and variance and log_pi = -inf (binding.cpp:82-90)."""
+    from flashgmm_b200 import flash_gmm_native as C
+    N, K, d = 64, 3, 5
+    X = torch.randn(N, d, generator=torch.Generator().manual_seed(0))
+    G = torch.rand(N, K, generator=torch.Generator().manual_seed(1))
+    G[:, 1] = 0.0
+    G = G / G.sum(1, keepdim=True)
+    mu, var, lp = [o.cpu() for o in C.standard_m_step(X.to(DEV), G.to(DEV))]
+    assert torch.isnan(mu[1]).all() and torch.isnan(var[1]).all() and lp[1] == -float("inf")
+    assert torch.isfinite(mu[[0, 2]]).all() and torch.isfinite(lp[[0, 2]]).all()
+
+
+def test_standard_model_matches_flash_model():
+    """NativeStandardGMM (E-step + M-step ops) and NativeFlashGMM (fused iteration)
+    follow the same trajectory from the same start."""
+    from flashgmm_b200.native_wrapper import NativeFlashGMM, NativeStandardGMM
+    g = load_golden("c3_slice4096")
+    X = _t(g["X"])
+    init = [_t(g[k]) for k in ("mu", "var", "log_pi")]
+    K, d = init[0].shape
+    hs = NativeStandardGMM(K, d, max_iter=8, tol=0.0).fit(X, init=init)
+    hf = NativeFlashGMM(K, d, max_iter=8, tol=0.0).fit(X, init=init)
+    lls = np.array([h["log_likelihood"] for h in hs])
+    llf = np.array([h["log_likelihood"] for h in hf])
+    assert np.max(np.abs(lls - llf)) < 1e-3
+
+
+def test_predict():
+    from flashgmm_b200.native_wrapper import NativeFlashGMM
+    g = load_golden("c1_iter1")
+    X = _t(g["X"])
+    m = NativeFlashGMM(g["mu"].shape[0], g["mu"].shape[1], max_iter=5)
+    m.fit(X)
+    p = m.predict_proba(X)
+    assert p.shape == (X.shape[0], g["mu"].shape[0])
+    assert torch.allclose(p.sum(1), torch.ones(X.shape[0], device=DEV), atol=1e-5)
+    assert torch.equal(m.predict(X), p.argmax(1))
