@@ -227,12 +227,6 @@ __device__ __forceinline__ bool drain_group(uint32_t lane_tmem, uint32_t &gcount
 }
 
 // ------------------------------------------------------------------------- pass 1
-#ifdef FGMM_EXP_TIMING1
-__device__ unsigned long long g_tim1[2048][8];
-#define T1TICK(v) do { unsigned long long _t = globaltimer(); v += _t - Tx1; Tx1 = _t; } while (0)
-#else
-#define T1TICK(v) do { } while (0)
-#endif
 template <int NKC>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ CUtensorMap tm_plo,
@@ -275,9 +269,6 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int n_units = n_pt * G;
-#ifdef FGMM_EXP_TIMING1
-  unsigned long long A1 = 0, B1 = 0, C1 = 0, D1 = 0, Tx1 = globaltimer(), T01 = Tx1;
-#endif
 
   if (warp == 0) {
     if (lane == 0) {
@@ -292,9 +283,7 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
         const int t1 = min(n_ct, (g + 1) * tpg);
         for (int t = g * tpg; t < t1 && ok; ++t) {
           for (int c = 0; c < NKC; ++c) {
-            T1TICK(B1);
             if (!mbar_wait(EMPTY(stage), phase ^ 1, kErrWaitEmpty)) { ok = false; break; }
-            T1TICK(A1);
             const uint32_t base = smem_u32(smem + stage * kStageBytes);
             mbar_arrive_expect_tx(FULL(stage), kStageBytes);
             tma_load_2d_hint(base, &tm_phi, c * KC, pt * BM, FULL(stage), pol_p);
@@ -321,15 +310,12 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
         const int t1 = min(n_ct, (g + 1) * tpg);
         for (int t = g * tpg; t < t1 && ok; ++t) {
           for (int c = 0; c < NKC; ++c) {
-            T1TICK(D1);
             if (!mbar_wait(FULL(stage), phase, kErrWaitFull)) { ok = false; break; }
-            T1TICK(A1);
             tc_fence_after();
             constexpr int GC = group_chunks<NKC>();
             if (!issue_dist_chunk<NB>(smem_u32(smem + stage * kStageBytes), tmem, gcount, TFULL0,
                                       TEMPTY0, c % GC == 0, c % GC == GC - 1)) { ok = false; break; }
             mma_commit(EMPTY(stage));
-            T1TICK(B1);
             if (++stage == S) { stage = 0; phase ^= 1; }
           }
         }
@@ -354,13 +340,10 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
       const int64_t n_row = (int64_t)pt * BM + row;
       for (int t = g * tpg; t < t1 && ok; ++t) {
         float acc[kPart];
-        T1TICK(D1);
         ok = drain_group<NB, true>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
-        T1TICK(C1);
 #pragma unroll 1
         for (int grp = 1; grp < NKC / group_chunks<NKC>() && ok; ++grp)
           ok = drain_group<NB, false>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
-        T1TICK(A1);
         if (!ok) break;
         const int kb = t * NC + part * kPart;
         float cst[kPart];
@@ -398,7 +381,6 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
           }
         }
       }
-      T1TICK(B1);
       // merge the column parts of each row
       if (part > 0) lse_x[(part - 1) * BM + row] = Part{m, s, v1, v2, i1, i2};
       ok = epi_sync_and(ok);
@@ -444,12 +426,6 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
-#ifdef FGMM_EXP_TIMING1
-  if (lane == 0 && warp < 4 && blockIdx.x < 512) {
-    unsigned long long *o = g_tim1[blockIdx.x * 4 + warp];
-    o[0] = A1; o[1] = B1; o[2] = C1; o[3] = D1; o[6] = globaltimer() - T01; o[7] = 1;
-  }
-#endif
 }
 
 // ------------------------------------------------------------------------- refine
@@ -628,9 +604,6 @@ __device__ __forceinline__ bool cta_sync_and(bool v) {
   return __syncthreads_and(v ? 1 : 0) != 0;
 }
 
-#ifdef FGMM_EXP_TIMING
-__device__ unsigned long long g_tim[2048][8];
-#endif
 // Partial statistics row (per component and CTA slot, partial[k][slot]):
 // [s (DP) | sq (DP) | n | pad], stride 2 DP + 4.
 template <int NKC>
@@ -730,12 +703,6 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
   };
 
   float nk = 0.0f;
-#ifdef FGMM_EXP_TIMING
-  unsigned long long Ta = 0, Tb = 0, Tc = 0, Td = 0, Te = 0, Tx = globaltimer(), Tk0 = Tx;
-#define TICK(v) do { unsigned long long _t = globaltimer(); v += _t - Tx; Tx = _t; } while (0)
-#else
-#define TICK(v) do { } while (0)
-#endif
   if (warp < kGammaWarps) {
     // ---------------- gamma warps
     const int p0 = (warp >> 2) * 8;  // this warp's 8 points of each slice
@@ -745,12 +712,9 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
       // this warp could need the MMA to have started tile j + NSR.
       while (nf < T && s >= kSlicesFlush * (nf + 1) + kGBufs && ok) flush_next(false);
       if (nf < T && s >= kSlicesFlush * (nf + 1) && tile_done(nf)) flush_next(false);  // early
-      TICK(Td);
       const int st = s % NST, gb = s % kGBufs;
       ok = ok && __all_sync(0xffffffffu, mbar_wait(FULL(st), (s / NST) & 1, kErrWaitFull));
-      TICK(Ta);
       ok = ok && __all_sync(0xffffffffu, mbar_wait(GEMPTY(gb), ((s / kGBufs) & 1) ^ 1, kErrWaitGammaEmpty));
-      TICK(Tb);
       if (!ok) break;
       tc_fence_after();
       const uint8_t *stg = smem + st * Sh::kStage;
@@ -786,7 +750,6 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(GFULL(gb));
-      TICK(Tc);
     }
   } else if (warp == kGammaWarps) {
     // ---------------- MMA warp
@@ -796,15 +759,11 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
       const bool tile_first = s % kSlicesFlush == 0;
       if (tile_first && j >= NSR) {
         while (nf <= j - NSR && ok) flush_next(false);
-        TICK(Te);
         ok = ok && __all_sync(0xffffffffu, mbar_wait(SEMPTY(reg), ((j / NSR) & 1) ^ 1, kErrWaitStatsDone));
       }
-      TICK(Td);
       const int st = s % NST, gb = s % kGBufs;
       ok = ok && __all_sync(0xffffffffu, mbar_wait(FULL(st), (s / NST) & 1, kErrWaitFull));
-      TICK(Ta);
       ok = ok && __all_sync(0xffffffffu, mbar_wait(GFULL(gb), (s / kGBufs) & 1, kErrWaitGammaFull));
-      TICK(Tb);
       if (!ok) break;
       if (lane == 0) {
         tc_fence_after();
@@ -828,7 +787,6 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
         if (s % kSlicesFlush == kSlicesFlush - 1 || s == S - 1) mma_commit(SFULL(reg));
       }
       __syncwarp();
-      TICK(Tc);
     }
     if (lane == 0 && S > 0) {  // every MMA of this CTA has completed before the teardown
       mma_commit(DONE);
@@ -849,9 +807,7 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
       while (nf < T && s >= kSlicesFlush * (nf + 1) + NST && ok) flush_next(false);
       if (nf < T && s >= kSlicesFlush * (nf + 1) && tile_done(nf)) flush_next(false);  // early
       const int st = s % NST;
-      TICK(Td);
       if (s >= NST) ok = ok && __all_sync(0xffffffffu, mbar_wait(EMPTY(st), ((s / NST) & 1) ^ 1, kErrWaitEmpty));
-      TICK(Ta);
       if (!ok) break;
       if (lane == 0) {
         const uint32_t base = smem_u32(smem + st * Sh::kStage);
@@ -905,12 +861,6 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
-#ifdef FGMM_EXP_TIMING
-  if (lane == 0 && (warp == 0 || warp == kGammaWarps || warp == kGammaWarps + 1) && blockIdx.x < 512) {
-    unsigned long long *o = g_tim[blockIdx.x * 4 + (warp == 0 ? 0 : warp - kGammaWarps + 1)];
-    o[0] = Ta; o[1] = Tb; o[2] = Tc; o[3] = Td; o[4] = Te; o[5] = 0; o[6] = globaltimer() - Tk0; o[7] = S;
-  }
-#endif
 }
 
 // ------------------------------------------------------------------------- host
@@ -1180,18 +1130,6 @@ int tc_em_stats(const float *X, const void *points, int64_t N, int d, const floa
                          refine_blocks(p.first.Nc), stats, st);
 }
 
-#ifdef FGMM_EXP_TIMING1
-extern "C" int fgmm_exp_timing1(unsigned long long *out, int n) {
-  cudaDeviceSynchronize();
-  return (int)cudaMemcpyFromSymbol(out, g_tim1, sizeof(unsigned long long) * 8 * n);
-}
-#endif
-#ifdef FGMM_EXP_TIMING
-extern "C" int fgmm_exp_timing(unsigned long long *out, int n) {
-  cudaDeviceSynchronize();
-  return (int)cudaMemcpyFromSymbol(out, g_tim, sizeof(unsigned long long) * 8 * n);
-}
-#endif
 int tc_device_error(bool reset) {
   int v = 0;
   if (cudaDeviceSynchronize() != cudaSuccess) return -1;
