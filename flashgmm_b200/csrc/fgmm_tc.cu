@@ -339,16 +339,19 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
       int i1 = -1, i2 = -1;
       const int64_t n_row = (int64_t)pt * BM + row;
       for (int t = g * tpg; t < t1 && ok; ++t) {
+        const int kb = t * NC + part * kPart;
+        // this warp's 32 log-coefficients: one load per lane, issued before the drains and
+        // handed out by shuffles
+        const float cv = __ldg(cst2 + kb + lane);
         float acc[kPart];
         ok = drain_group<NB, true>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
 #pragma unroll 1
         for (int grp = 1; grp < NKC / group_chunks<NKC>() && ok; ++grp)
           ok = drain_group<NB, false>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
         if (!ok) break;
-        const int kb = t * NC + part * kPart;
         float cst[kPart];
 #pragma unroll
-        for (int e = 0; e < kPart; ++e) cst[e] = __ldg(cst2 + kb + e);
+        for (int e = 0; e < kPart; ++e) cst[e] = __shfl_sync(0xffffffffu, cv, e);
         float c4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
 #pragma unroll
         for (int e = 0; e < kPart; ++e) {
