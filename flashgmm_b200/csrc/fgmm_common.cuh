@@ -22,6 +22,29 @@ int cuda_fail(cudaError_t e, const char *what);
     if (_e != cudaSuccess) return ::fgmm::cuda_fail(_e, #expr); \
   } while (0)
 
+// Programmatic dependent launch: the kernel may be scheduled while its predecessor on the
+// stream is still finishing (its launch and set-up overlap the predecessor's tail).  Every
+// kernel launched this way calls griddep_wait() before it touches global memory that
+// earlier work on the stream reads or writes, and griddep_launch() once all its blocks
+// have been scheduled, so the next kernel can start setting up.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 #define FGMM_LAUNCH_CHECK(what)                               \
   do {                                                        \
     cudaError_t _e = cudaGetLastError();                      \

@@ -99,6 +99,8 @@ __global__ void tc_prep_params_kernel(const float *__restrict__ mu, const float 
                                       float *__restrict__ qhi, float *__restrict__ qlo,
                                       float *__restrict__ cst2, float *__restrict__ sc,
                                       float *__restrict__ ms, float *__restrict__ lc) {
+  griddep_launch();
+  griddep_wait();
   const int k = blockIdx.x;
   const int KA = 2 * dp;
   __shared__ double red[8], red2[8];
@@ -267,6 +269,8 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  griddep_launch();
+  griddep_wait();  // the parameter operands and Lt of earlier launches
   const uint32_t tmem = *tmem_slot;
   const int n_units = n_pt * G;
 
@@ -453,6 +457,8 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
                  float *__restrict__ ln2x, float *__restrict__ Lt, int64_t Npad,
                  float *__restrict__ ln_out, double *__restrict__ ln_part, int acc_ln) {
   __shared__ double wsum[8];
+  griddep_launch();
+  griddep_wait();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int sub = lane & 7;           // lane within the point's group of 8
   double acc = 0.0;
@@ -660,6 +666,8 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  griddep_launch();
+  griddep_wait();  // Lt, ln2x and the partial rows of earlier launches
   const uint32_t tmem = *tmem_slot;
 
   const int q = warp & 3, seg = warp >> 2;  // TMEM lane quarter, column segment
@@ -1024,10 +1032,9 @@ int tc_launch_chunk(const TcPlan &p, const TcChunk &c, int64_t n0, bool first, c
   if ((rc = make_map(&m_plo, plo, rows, p.KA, BM))) return rc;
   if ((rc = make_map(&m_qhi, w.qhi, p.Kp, p.KA, NC))) return rc;
   if ((rc = make_map(&m_qlo, w.qlo, p.Kp, p.KA, NC))) return rc;
-  tc_pass1_kernel<NKC><<<c.grid1, kThreads, smem1_bytes(), st>>>(
-      m_phi, m_plo, m_qhi, m_qlo, w.cst2, c.Nc, c.n_pt, p.n_ct, c.G, c.tpg, w.part_m, w.part_s,
-      w.part_tv, w.part_ti, w.L, lcols);
-  FGMM_LAUNCH_CHECK("tc_pass1_kernel");
+  FGMM_CUDA_TRY(launch_pdl(tc_pass1_kernel<NKC>, c.grid1, kThreads, smem1_bytes(), st, m_phi, m_plo,
+                           m_qhi, m_qlo, w.cst2, c.Nc, c.n_pt, p.n_ct, c.G, c.tpg, w.part_m,
+                           w.part_s, w.part_tv, w.part_ti, w.L, lcols));
   mark(st, "tc_pass1_kernel");
   {
     const int blocks = refine_blocks(c.Nc);
@@ -1037,15 +1044,13 @@ int tc_launch_chunk(const TcPlan &p, const TcChunk &c, int64_t n0, bool first, c
 #define FGMM_REFINE(D)                                                                             \
   do {                                                                                             \
     if (vec && (D) % 4 == 0 && 8 * (D) == p.d)                                                     \
-      tc_refine_kernel<D, true><<<blocks, 256, 0, st>>>(Xc, c.Nc, p.d, w.sc, w.ms, w.lc, w.part_m, \
-                                                        w.part_s, w.part_tv, w.part_ti, c.G,       \
-                                                        w.ln2x, w.L, lcols, ln + n0, w.ln_part,    \
-                                                        acc);                                      \
+      FGMM_CUDA_TRY(launch_pdl(tc_refine_kernel<D, true>, blocks, 256, 0, st, Xc, c.Nc, p.d, w.sc, \
+                               w.ms, w.lc, w.part_m, w.part_s, w.part_tv, w.part_ti, c.G, w.ln2x,  \
+                               w.L, lcols, ln + n0, w.ln_part, acc));                              \
     else                                                                                           \
-      tc_refine_kernel<D, false><<<blocks, 256, 0, st>>>(Xc, c.Nc, p.d, w.sc, w.ms, w.lc,          \
-                                                         w.part_m, w.part_s, w.part_tv,            \
-                                                         w.part_ti, c.G, w.ln2x, w.L, lcols,       \
-                                                         ln + n0, w.ln_part, acc);                 \
+      FGMM_CUDA_TRY(launch_pdl(tc_refine_kernel<D, false>, blocks, 256, 0, st, Xc, c.Nc, p.d, w.sc,\
+                               w.ms, w.lc, w.part_m, w.part_s, w.part_tv, w.part_ti, c.G, w.ln2x,  \
+                               w.L, lcols, ln + n0, w.ln_part, acc));                              \
   } while (0)
     if (dpl <= 1) FGMM_REFINE(1);
     else if (dpl <= 2) FGMM_REFINE(2);
@@ -1061,9 +1066,8 @@ int tc_launch_chunk(const TcPlan &p, const TcChunk &c, int64_t n0, bool first, c
   if ((rc = make_map_atoms(&m_fhi, phi, rows, p.KA, kSlicePts))) return rc;
   if ((rc = make_map_atoms(&m_flo, plo, rows, p.KA, kSlicePts))) return rc;
   if ((rc = make_map(&m_l, w.L, p.Kp, (int)lcols, NC, CU_TENSOR_MAP_SWIZZLE_64B, kSlicePts))) return rc;
-  tc_stats_kernel<NKC><<<c.grid2, kThreads2, smem2_bytes(NKC * KC), st>>>(
-      m_fhi, m_flo, m_l, w.ln2x, c.Nc, c.S, p.K, w.partial, first ? 0 : 1);
-  FGMM_LAUNCH_CHECK("tc_stats_kernel");
+  FGMM_CUDA_TRY(launch_pdl(tc_stats_kernel<NKC>, c.grid2, kThreads2, smem2_bytes(NKC * KC), st,
+                           m_fhi, m_flo, m_l, w.ln2x, c.Nc, c.S, p.K, w.partial, first ? 0 : 1));
   mark(st, "tc_stats_kernel");
   return FGMM_OK;
 }
@@ -1115,9 +1119,8 @@ int tc_em_stats(const float *X, const void *points, int64_t N, int d, const floa
                 void *ws, cudaStream_t st) {
   const TcPlan p = plan(N, d, K);
   const TcWs w = tc_layout(ws, p);
-  tc_prep_params_kernel<<<p.Kp, 128, 0, st>>>(mu, var, log_pi, K, d, p.dp, w.qhi, w.qlo, w.cst2,
-                                               w.sc, w.ms, w.lc);
-  FGMM_LAUNCH_CHECK("tc_prep_params_kernel");
+  FGMM_CUDA_TRY(launch_pdl(tc_prep_params_kernel, p.Kp, 128, 0, st, mu, var, log_pi, K, d, p.dp,
+                           w.qhi, w.qlo, w.cst2, w.sc, w.ms, w.lc));
   mark(st, "tc_prep_params_kernel");
   const float *pts = static_cast<const float *>(points);
   int rc;

@@ -22,6 +22,8 @@ __global__ void __launch_bounds__(32 * kRedGroups, 6)  // six blocks (1536 threa
 reduce_partials_kernel(const float *__restrict__ part, int slots, int K, int d, int ds, int W,
                        const double *__restrict__ lnp, int ln_slots, double *__restrict__ stats) {
   __shared__ double sh[kRedGroups][32];
+  griddep_launch();
+  griddep_wait();
   const int V = 2 * d + 1;
   const int64_t total = (int64_t)K * V;
   const int64_t slot_stride = W;
@@ -77,9 +79,8 @@ int reduce_partials(const float *partials, int slots, int K, int d, int ds, int 
 #define FGMM_RED_BLOCKS_PER_SM 16
 #endif
   int blocks = (int)std::min<int64_t>(cdiv(total, 32), FGMM_RED_BLOCKS_PER_SM * num_sms());
-  reduce_partials_kernel<<<blocks, 32 * kRedGroups, 0, stream>>>(partials, slots, K, d, ds, W,
-                                                                 ln_partials, ln_slots, stats);
-  FGMM_LAUNCH_CHECK("reduce_partials_kernel");
+  FGMM_CUDA_TRY(launch_pdl(reduce_partials_kernel, blocks, 32 * kRedGroups, 0, stream, partials,
+                           slots, K, d, ds, W, ln_partials, ln_slots, stats));
   mark(stream, "reduce_partials_kernel");
   return FGMM_OK;
 }
@@ -91,6 +92,8 @@ int reduce_partials(const float *partials, int slots, int K, int d, int ds, int 
 __global__ void em_update_kernel(const double *__restrict__ stats, double n_total, int K, int d,
                                  float *__restrict__ new_mu, float *__restrict__ new_var,
                                  float *__restrict__ new_log_pi, int floors) {
+  griddep_launch();
+  griddep_wait();
   const int k = blockIdx.x;
   const double nk = stats[k];
   const double inv = 1.0 / (floors ? fmax(nk, 1e-8) : nk);
@@ -109,9 +112,8 @@ __global__ void em_update_kernel(const double *__restrict__ stats, double n_tota
 int em_update(const double *stats, double n_total, int K, int d, float *new_mu, float *new_var,
               float *new_log_pi, cudaStream_t stream, bool floors) {
   int threads = d >= 128 ? 128 : (d >= 64 ? 64 : 32);
-  em_update_kernel<<<K, threads, 0, stream>>>(stats, n_total, K, d, new_mu, new_var, new_log_pi,
-                                              floors ? 1 : 0);
-  FGMM_LAUNCH_CHECK("em_update_kernel");
+  FGMM_CUDA_TRY(launch_pdl(em_update_kernel, K, threads, 0, stream, stats, n_total, K, d, new_mu,
+                           new_var, new_log_pi, floors ? 1 : 0));
   return FGMM_OK;
 }
 
