@@ -446,8 +446,18 @@ def run_e2e(wl, dev, args, ws_n=1, rank=0, steps=200):
         dt = t.item()
     h2d = Xh.numel() * 4 + sum(t.numel() * 4 for t in ph)
     d2h = sum(t.numel() * 4 for t in out_h)
+    # the copy-only bound: this rank's X shard over PCIe from pinned memory, timed alone
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    Xd[0].copy_(Xh, non_blocking=True)
+    e0.record()
+    for _ in range(5):
+        Xd[0].copy_(Xh, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    h2d_gbs = 5 * Xh.numel() * 4 / (e0.elapsed_time(e1) * 1e-3) / 1e9
     return {"value": ws_n / dt, "unit": "iter/s", "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h,
+            "d2h_bytes_per_step": d2h, "h2d_gbs": h2d_gbs,
+            "copy_bound_iter_s": ws_n * h2d_gbs * 1e9 / h2d,
             "step": ("H2D of X and the parameters from pinned host memory, one EM iteration "
                      "through flashgmm_b200.flash_gmm_native, D2H of the new parameters and "
                      "log-normalizer; X copies double-buffered on a second stream (per-rank "
