@@ -298,9 +298,11 @@ def run_ours(args, wl):
 
     def step():
         nonlocal mu, var, lp
+        if ws_n == 1:  # statistics and update in one call (update fused into the reduction)
+            C.em_step(X, mu, var, lp, points=points, workspace=ws, out=(mu, var, lp))
+            return
         stats, _ = C.em_stats(X, mu, var, lp, points=points, workspace=ws)
-        if ws_n > 1:
-            dist.all_reduce(stats)
+        dist.all_reduce(stats)
         mu, var, lp = C.em_update(stats, n_total, K, d)
 
     clocks = ClockSampler(gpu_id(dev)).start() if rank == 0 else None
@@ -353,7 +355,7 @@ def run_ours(args, wl):
         "algorithmic": {"flops_per_iter": flops, "bytes_per_iter": nbytes,
                         "dominant_flops_per_launch": flops / 2.0 if gemm else None}})
 
-    launches = lib.fgmm_em_stats_launches(N, d, K) + 1
+    launches = lib.fgmm_em_stats_launches(N, d, K) + (1 if ws_n > 1 else 0)
     e2e = None
     cpu = None
     if not args.no_e2e:

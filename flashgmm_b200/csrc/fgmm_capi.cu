@@ -99,9 +99,12 @@ size_t fgmm_em_stats_workspace_bytes(int64_t N, int32_t d, int32_t K) {
   return 0;
 }
 
-int fgmm_em_stats(const float *X, const void *points, int64_t N, int32_t d, const float *mu,
+namespace {
+// fgmm_em_stats, optionally with the M-step applied in the statistics reduction's launch.
+int em_stats_impl(const float *X, const void *points, int64_t N, int32_t d, const float *mu,
                   const float *var, const float *log_pi, int32_t K, double *stats,
-                  float *log_normalizer, void *workspace, size_t workspace_bytes, void *stream) {
+                  float *log_normalizer, void *workspace, size_t workspace_bytes, void *stream,
+                  const fgmm::UpdateOut *update) {
   int rc = check_shape(N, d, K);
   if (rc) return rc;
   if (!X || !mu || !var || !log_pi || !stats || !log_normalizer || !workspace)
@@ -114,7 +117,7 @@ int fgmm_em_stats(const float *X, const void *points, int64_t N, int32_t d, cons
   if (fam == FGMM_FAMILY_SIMT) {
     if (workspace_bytes < simt_workspace_bytes(N, d, K))
       return fail(FGMM_ERR_WORKSPACE, "workspace too small");
-    return simt_em_stats(X, N, d, mu, var, log_pi, K, stats, log_normalizer, workspace, st);
+    return simt_em_stats(X, N, d, mu, var, log_pi, K, stats, log_normalizer, workspace, st, update);
   }
   size_t need = tc_workspace_bytes(N, d, K);
   const void *pts = points;
@@ -129,7 +132,25 @@ int fgmm_em_stats(const float *X, const void *points, int64_t N, int32_t d, cons
   } else if (workspace_bytes < need) {
     return fail(FGMM_ERR_WORKSPACE, "workspace too small");
   }
-  return tc_em_stats(X, pts, N, d, mu, var, log_pi, K, stats, log_normalizer, workspace, st);
+  return tc_em_stats(X, pts, N, d, mu, var, log_pi, K, stats, log_normalizer, workspace, st, update);
+}
+}  // namespace
+
+int fgmm_em_stats(const float *X, const void *points, int64_t N, int32_t d, const float *mu,
+                  const float *var, const float *log_pi, int32_t K, double *stats,
+                  float *log_normalizer, void *workspace, size_t workspace_bytes, void *stream) {
+  return em_stats_impl(X, points, N, d, mu, var, log_pi, K, stats, log_normalizer, workspace,
+                       workspace_bytes, stream, nullptr);
+}
+
+int fgmm_em_step(const float *X, const void *points, int64_t N, int32_t d, const float *mu,
+                 const float *var, const float *log_pi, int32_t K, float *new_mu, float *new_var,
+                 float *new_log_pi, double *stats, float *log_normalizer, void *workspace,
+                 size_t workspace_bytes, void *stream) {
+  if (!new_mu || !new_var || !new_log_pi) return fail(FGMM_ERR_INVALID, "null pointer argument");
+  const fgmm::UpdateOut up{(double)N, new_mu, new_var, new_log_pi, true};
+  return em_stats_impl(X, points, N, d, mu, var, log_pi, K, stats, log_normalizer, workspace,
+                       workspace_bytes, stream, &up);
 }
 
 int fgmm_em_update(const double *stats, double n_total, int32_t K, int32_t d, float *new_mu,
@@ -161,10 +182,10 @@ int fgmm_em_fused(const float *X, int64_t N, int32_t d, const float *mu, const f
   // stats live at the end; the stats workspace (+ in-place points) at the front
   const size_t stats_off = need - align_up((size_t)fgmm_stats_len(K, d) * sizeof(double), 256);
   double *stats = reinterpret_cast<double *>(static_cast<char *>(workspace) + stats_off);
-  rc = fgmm_em_stats(X, nullptr, N, d, mu, var, log_pi, K, stats, log_normalizer, workspace,
-                     stats_off, stream);
-  if (rc) return rc;
-  return fgmm_em_update(stats, (double)N, K, d, new_mu, new_var, new_log_pi, stream);
+  if (!new_mu || !new_var || !new_log_pi) return fail(FGMM_ERR_INVALID, "null pointer");
+  const fgmm::UpdateOut up{(double)N, new_mu, new_var, new_log_pi, true};
+  return em_stats_impl(X, nullptr, N, d, mu, var, log_pi, K, stats, log_normalizer, workspace,
+                       stats_off, stream, &up);
 }
 
 size_t fgmm_e_step_workspace_bytes(int64_t N, int32_t d, int32_t K) {

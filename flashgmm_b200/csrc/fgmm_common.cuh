@@ -39,7 +39,11 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
+#ifdef FGMM_NO_PDL
+  cfg.numAttrs = 0;
+#else
   cfg.numAttrs = 1;
+#endif
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -89,11 +93,18 @@ inline void mark(cudaStream_t st, const char *name) {
 int simt_launches();
 int tc_launches(int64_t N, int d, int K);
 
+// Where the M-step is applied in the same launch as the statistics reduction.
+struct UpdateOut {
+  double n_total;
+  float *mu, *var, *log_pi;
+  bool floors;
+};
+
 // ---- SIMT family (fgmm_simt.cu) ----
 size_t simt_workspace_bytes(int64_t N, int d, int K);
 int simt_em_stats(const float *X, int64_t N, int d, const float *mu, const float *var,
                   const float *log_pi, int K, double *stats, float *log_norm,
-                  void *ws, cudaStream_t stream);
+                  void *ws, cudaStream_t stream, const UpdateOut *update = nullptr);
 
 // ---- tcgen05 family (fgmm_tc.cu) ----
 bool tc_supported(int64_t N, int d, int K);
@@ -104,14 +115,15 @@ int tc_prepare_points(const float *X, int64_t N, int d, void *points, cudaStream
 int tc_device_error(bool reset);
 int tc_em_stats(const float *X, const void *points, int64_t N, int d, const float *mu,
                 const float *var, const float *log_pi, int K, double *stats,
-                float *log_norm, void *ws, cudaStream_t stream);
+                float *log_norm, void *ws, cudaStream_t stream, const UpdateOut *update = nullptr);
 
 // ---- shared epilogue kernels (fgmm_update.cu) ----
-// Sums per-block fp32 partials [slots][K][W] (rows [s (ds) | sq (ds) | n ...]) and
-// per-block log-normalizer sums into the packed fp64 stats vector (one launch).
+// Sums per-block fp32 partials [K][slots][W] (rows [s (ds) | sq (ds) | n ...]) and
+// per-block log-normalizer sums into the packed fp64 stats vector (one launch); with
+// `update`, also writes the updated parameters.
 int reduce_partials(const float *partials, int slots, int K, int d, int ds, int W,
                     const double *ln_partials, int ln_slots, double *stats,
-                    cudaStream_t stream);
+                    cudaStream_t stream, const UpdateOut *update = nullptr);
 int em_update(const double *stats, double n_total, int K, int d, float *new_mu,
               float *new_var, float *new_log_pi, cudaStream_t stream, bool floors = true);
 

@@ -69,7 +69,6 @@ extern "C" int fgmm_em_fused_static(const float *X, int64_t N, int32_t d, const 
   if (rc) return rc;
   cudaStream_t st = (cudaStream_t)stream;
   double *stats_ptr = reinterpret_cast<double *>(static_cast<char *>(scratch) + ws);
-  rc = simt_em_stats(X, N, d, mu, var, log_pi, K, stats_ptr, log_normalizer, scratch, st);
-  if (rc) return rc;
-  return em_update(stats_ptr, (double)N, K, d, new_mu, new_var, new_log_pi, st);
+  const UpdateOut up{(double)N, new_mu, new_var, new_log_pi, true};
+  return simt_em_stats(X, N, d, mu, var, log_pi, K, stats_ptr, log_normalizer, scratch, st, &up);
 }

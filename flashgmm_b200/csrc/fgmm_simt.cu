@@ -326,7 +326,7 @@ size_t simt_workspace_bytes(int64_t N, int d, int K) { return simt_layout(nullpt
 
 int simt_em_stats(const float *X, int64_t N, int d, const float *mu, const float *var,
                   const float *log_pi, int K, double *stats, float *log_norm, void *ws,
-                  cudaStream_t st) {
+                  cudaStream_t st, const UpdateOut *update) {
   SimtWs w = simt_layout(ws, N, d, K);
   simt_prep_kernel<<<K, 64, 0, st>>>(mu, var, log_pi, K, d, w.sc, w.ms, w.lc);
   FGMM_LAUNCH_CHECK("simt_prep_kernel");
@@ -342,7 +342,8 @@ int simt_em_stats(const float *X, int64_t N, int d, const float *mu, const float
     default: rc = simt_launch<8>(X, N, d, K, w, log_norm, st); break;
   }
   if (rc != FGMM_OK) return rc;
-  return reduce_partials(w.partial, w.slots, K, d, d, 2 * d + 1, w.ln_part, w.p1_blocks, stats, st);
+  return reduce_partials(w.partial, w.slots, K, d, d, 2 * d + 1, w.ln_part, w.p1_blocks, stats, st,
+                         update);
 }
 
 }  // namespace fgmm

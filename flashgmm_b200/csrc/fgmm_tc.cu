@@ -490,21 +490,21 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
     if (j2 >= 0 && b2 < b1 - 40.0f) j2 = -1;
     const int k1 = j1 >= 0 ? j1 : 0, k2 = j2 >= 0 ? j2 : 0;
     const bool need2 = __any_sync(0xffffffffu, j2 >= 0);
-    // lane `sub` takes the DPL consecutive dimensions starting at sub * DPL
+    // the 8 lanes of a point read each row in consecutive 16-byte (VEC) or 4-byte pieces,
+    // so a load instruction of the warp touches whole 128-byte lines
     float x[DPL], s1[DPL], m1[DPL], s2[DPL], m2[DPL];
     const bool use2 = need2 && j2 >= 0;
-    const int j0 = sub * DPL;
-    if (VEC) {  // d == 8 DPL, DPL % 4 == 0, 16-byte aligned rows
-      const float4 *xp = reinterpret_cast<const float4 *>(X + nn * d + j0);
-      const float4 *s1p = reinterpret_cast<const float4 *>(sc + (int64_t)k1 * d + j0);
-      const float4 *m1p = reinterpret_cast<const float4 *>(ms + (int64_t)k1 * d + j0);
-      const float4 *s2p = reinterpret_cast<const float4 *>(sc + (int64_t)k2 * d + j0);
-      const float4 *m2p = reinterpret_cast<const float4 *>(ms + (int64_t)k2 * d + j0);
+    if (VEC) {  // d == 8 DPL, DPL % 4 == 0, 16-byte aligned rows; lane takes float4 i * 8 + sub
+      const float4 *xp = reinterpret_cast<const float4 *>(X + nn * d) + sub;
+      const float4 *s1p = reinterpret_cast<const float4 *>(sc + (int64_t)k1 * d) + sub;
+      const float4 *m1p = reinterpret_cast<const float4 *>(ms + (int64_t)k1 * d) + sub;
+      const float4 *s2p = reinterpret_cast<const float4 *>(sc + (int64_t)k2 * d) + sub;
+      const float4 *m2p = reinterpret_cast<const float4 *>(ms + (int64_t)k2 * d) + sub;
 #pragma unroll
       for (int i = 0; i < DPL / 4; ++i) {
-        const float4 a = __ldg(xp + i), b = __ldg(s1p + i), c = __ldg(m1p + i);
-        const float4 e = use2 ? __ldg(s2p + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-        const float4 f = use2 ? __ldg(m2p + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 a = __ldg(xp + 8 * i), b = __ldg(s1p + 8 * i), c = __ldg(m1p + 8 * i);
+        const float4 e = use2 ? __ldg(s2p + 8 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 f = use2 ? __ldg(m2p + 8 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
         x[4 * i] = a.x; x[4 * i + 1] = a.y; x[4 * i + 2] = a.z; x[4 * i + 3] = a.w;
         s1[4 * i] = b.x; s1[4 * i + 1] = b.y; s1[4 * i + 2] = b.z; s1[4 * i + 3] = b.w;
         m1[4 * i] = c.x; m1[4 * i + 1] = c.y; m1[4 * i + 2] = c.z; m1[4 * i + 3] = c.w;
@@ -514,7 +514,7 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
     } else {
 #pragma unroll
       for (int i = 0; i < DPL; ++i) {
-        const int j = j0 + i;
+        const int j = i * 8 + sub;
         const bool in = j < d;
         x[i] = in ? __ldg(X + nn * d + j) : 0.0f;
         s1[i] = in ? __ldg(sc + (int64_t)k1 * d + j) : 0.0f;
@@ -1116,7 +1116,7 @@ int tc_prepare_points(const float *X, int64_t N, int d, void *points, cudaStream
 
 int tc_em_stats(const float *X, const void *points, int64_t N, int d, const float *mu,
                 const float *var, const float *log_pi, int K, double *stats, float *log_norm,
-                void *ws, cudaStream_t st) {
+                void *ws, cudaStream_t st, const UpdateOut *update) {
   const TcPlan p = plan(N, d, K);
   const TcWs w = tc_layout(ws, p);
   FGMM_CUDA_TRY(launch_pdl(tc_prep_params_kernel, p.Kp, 128, 0, st, mu, var, log_pi, K, d, p.dp,
@@ -1133,7 +1133,7 @@ int tc_em_stats(const float *X, const void *points, int64_t N, int d, const floa
   }
   if (rc) return rc;
   return reduce_partials(w.partial, p.first.S, K, d, p.dp, 2 * p.dp + 4, w.ln_part,
-                         refine_blocks(p.first.Nc), stats, st);
+                         refine_blocks(p.first.Nc), stats, st, update);
 }
 
 int tc_device_error(bool reset) {

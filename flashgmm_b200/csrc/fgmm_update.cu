@@ -9,78 +9,118 @@
 namespace fgmm {
 
 // partials: [K][slots][W] fp32 (a component's rows contiguous), each row laid out
-// [s (ds) | sq (ds) | n | ...] where only
-// the first d of each ds-wide run are meaningful; stats: [n (K) | s (K d) | sq (K d) | sum ln].
-// A block takes 32 consecutive output values (lane = value, so the loads of a warp are
-// contiguous) and splits the slots over its 8 warps (warp g sums slots g, g + 8, ... with
-// every load in flight before the adds); the 8 warp sums are then added in a fixed order,
-// so the result does not depend on timing.  Block 0 also sums the per-block
-// log-normalizer partials into the last entry.
-constexpr int kRedGroups = 8;
-constexpr int kRedUnroll = 10;  // loads in flight per thread (one round trip up to 80 slots)
-__global__ void __launch_bounds__(32 * kRedGroups, 6)  // six blocks (1536 threads) per SM
+// [s (ds) | sq (ds) | n | ...] where only the first d of each ds-wide run are meaningful;
+// stats: [n (K) | s (K d) | sq (K d) | sum ln].
+// One block per component (block K sums the per-block log-normalizer partials).  The
+// 512 threads are G slot groups x DT dimension lanes: thread (g, j) sums dimension j's
+// s and sq over slots g, g + G, ... with kRedBatch slots' loads in flight, so a warp reads
+// 128 contiguous bytes per load; warp 0 first sums n_k.  The G group sums are added in a
+// fixed order (deterministic) in fp64.  With `up`, the same block then applies the
+// M-step to its component (em_update_kernel's arithmetic), which saves the update launch.
+constexpr int kRedThreads = 512;
+constexpr int kRedBatch = 8;
+struct UpdateArgs {
+  double n_total;
+  float *mu, *var, *log_pi;
+  int floors, on;
+};
+
+__device__ __forceinline__ void update_component(double nk, double s, double q, double n_total,
+                                                 int floors, float *mu, float *var) {
+  const double inv = 1.0 / (floors ? fmax(nk, 1e-8) : nk);
+  const double m = s * inv;
+  const double v = q * inv - m * m;
+  *mu = (float)m;
+  *var = (float)(v < 1e-6 ? 1e-6 : v);
+}
+
+__global__ void __launch_bounds__(kRedThreads)
 reduce_partials_kernel(const float *__restrict__ part, int slots, int K, int d, int ds, int W,
-                       const double *__restrict__ lnp, int ln_slots, double *__restrict__ stats) {
-  __shared__ double sh[kRedGroups][32];
+                       const double *__restrict__ lnp, int ln_slots, double *__restrict__ stats,
+                       UpdateArgs up) {
+  __shared__ double sh_s[kRedThreads], sh_q[kRedThreads];
+  __shared__ double sh_n;
   griddep_launch();
   griddep_wait();
-  const int V = 2 * d + 1;
-  const int64_t total = (int64_t)K * V;
-  const int64_t slot_stride = W;
-  const int lane = threadIdx.x & 31, g = threadIdx.x >> 5;
-  for (int64_t base = (int64_t)blockIdx.x * 32; base < total; base += (int64_t)gridDim.x * 32) {
-    const int64_t i = base + lane;
-    const bool live = i < total;
-    const int k = live ? (int)(i / V) : 0, c = live ? (int)(i % V) : 0;
-    const int src = c < d ? c : (c < 2 * d ? ds + (c - d) : 2 * ds);
-    const float *p = part + (int64_t)k * slots * W + src;
-    double acc = 0.0;
-    const int n_mine = live && g < slots ? (slots - g + kRedGroups - 1) / kRedGroups : 0;
-    const float *q = p + (int64_t)g * slot_stride;
-    const int step = kRedGroups * (int)slot_stride;
-    for (int s = 0; s < n_mine; s += kRedUnroll) {  // all loads of a batch, then the adds
-      float v[kRedUnroll];
+  const int k = blockIdx.x, t = threadIdx.x, lane = t & 31;
+  if (k == K) {  // the log-normalizer sum
+    double a = 0.0;
+    for (int j = t; j < ln_slots; j += kRedThreads) a += lnp[j];
 #pragma unroll
-      for (int u = 0; u < kRedUnroll; ++u) v[u] = s + u < n_mine ? __ldg(q + (s + u) * step) : 0.0f;
-#pragma unroll
-      for (int u = 0; u < kRedUnroll; ++u) acc += (double)v[u];
-    }
-    sh[g][lane] = acc;
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    if (lane == 0) sh_s[t >> 5] = a;
     __syncthreads();
-    if (g == 0 && live) {
-      double t = 0.0;
+    if (t == 0) {
+      double tot = 0.0;
+      for (int w = 0; w < kRedThreads / 32; ++w) tot += sh_s[w];
+      stats[K + 2 * (int64_t)K * d] = tot;
+    }
+    return;
+  }
+  const float *pk = part + (int64_t)k * slots * W;
+  if (t < 32) {  // n_k: lanes over slots, fixed-order tree
+    double a = 0.0;
+    for (int sl = lane; sl < slots; sl += 32) a += (double)__ldg(pk + (int64_t)sl * W + 2 * ds);
 #pragma unroll
-      for (int u = 0; u < kRedGroups; ++u) t += sh[u][lane];
-      const int64_t dst = c < d ? K + (int64_t)k * d + c
-                        : (c < 2 * d ? K + (int64_t)K * d + (int64_t)k * d + (c - d) : (int64_t)k);
-      stats[dst] = t;
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    if (lane == 0) sh_n = a;
+  }
+  const int DT = d >= 128 ? 128 : (d + 31) / 32 * 32;  // dimension lanes
+  const int G = kRedThreads / DT;                        // slot groups
+  const int g = t / DT, jl = t - g * DT;
+  for (int j0 = 0; j0 < d; j0 += DT) {
+    const int j = j0 + jl;
+    double as = 0.0, aq = 0.0;
+    if (j < d) {
+      const float *ps = pk + j, *pq = pk + ds + j;
+      for (int sl = g; sl < slots; sl += G * kRedBatch) {
+        float vs[kRedBatch], vq[kRedBatch];
+#pragma unroll
+        for (int u = 0; u < kRedBatch; ++u) {
+          const int su = sl + u * G;
+          vs[u] = su < slots ? __ldg(ps + (int64_t)su * W) : 0.0f;
+          vq[u] = su < slots ? __ldg(pq + (int64_t)su * W) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < kRedBatch; ++u) { as += (double)vs[u]; aq += (double)vq[u]; }
+      }
+    }
+    sh_s[t] = as;
+    sh_q[t] = aq;
+    __syncthreads();
+    if (g == 0 && j < d) {
+      double s = 0.0, q = 0.0;
+      for (int u = 0; u < G; ++u) { s += sh_s[u * DT + jl]; q += sh_q[u * DT + jl]; }
+      stats[K + (int64_t)k * d + j] = s;
+      stats[K + (int64_t)K * d + (int64_t)k * d + j] = q;
+      if (up.on)
+        update_component(sh_n, s, q, up.n_total, up.floors, up.mu + (int64_t)k * d + j,
+                         up.var + (int64_t)k * d + j);
     }
     __syncthreads();
   }
-  if (blockIdx.x == 0) {
-    double a = 0.0;
-    for (int j = threadIdx.x; j < ln_slots; j += blockDim.x) a += lnp[j];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-    if (lane == 0) sh[g][0] = a;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      double t = 0.0;
-      for (int u = 0; u < kRedGroups; ++u) t += sh[u][0];
-      stats[total] = t;
-    }
+  if (t == 0) {
+    const double nk = sh_n;
+    stats[k] = nk;
+    if (up.on)
+      up.log_pi[k] = (float)(up.floors ? log(fmax(nk / up.n_total, 1e-8)) : log(nk / up.n_total));
   }
 }
 
 int reduce_partials(const float *partials, int slots, int K, int d, int ds, int W,
-                    const double *ln_partials, int ln_slots, double *stats, cudaStream_t stream) {
-  const int64_t total = (int64_t)K * (2 * d + 1);
-#ifndef FGMM_RED_BLOCKS_PER_SM
-#define FGMM_RED_BLOCKS_PER_SM 16
-#endif
-  int blocks = (int)std::min<int64_t>(cdiv(total, 32), FGMM_RED_BLOCKS_PER_SM * num_sms());
-  FGMM_CUDA_TRY(launch_pdl(reduce_partials_kernel, blocks, 32 * kRedGroups, 0, stream, partials,
-                           slots, K, d, ds, W, ln_partials, ln_slots, stats));
+                    const double *ln_partials, int ln_slots, double *stats, cudaStream_t stream,
+                    const UpdateOut *update) {
+  UpdateArgs up{};
+  if (update) {
+    up.n_total = update->n_total;
+    up.mu = update->mu;
+    up.var = update->var;
+    up.log_pi = update->log_pi;
+    up.floors = update->floors ? 1 : 0;
+    up.on = 1;
+  }
+  FGMM_CUDA_TRY(launch_pdl(reduce_partials_kernel, K + 1, kRedThreads, 0, stream, partials, slots,
+                           K, d, ds, W, ln_partials, ln_slots, stats, up));
   mark(stream, "reduce_partials_kernel");
   return FGMM_OK;
 }
@@ -96,15 +136,11 @@ __global__ void em_update_kernel(const double *__restrict__ stats, double n_tota
   griddep_wait();
   const int k = blockIdx.x;
   const double nk = stats[k];
-  const double inv = 1.0 / (floors ? fmax(nk, 1e-8) : nk);
   const double *s = stats + K + (int64_t)k * d;
   const double *q = stats + K + (int64_t)K * d + (int64_t)k * d;
-  for (int j = threadIdx.x; j < d; j += blockDim.x) {
-    const double m = s[j] * inv;
-    const double v = q[j] * inv - m * m;
-    new_mu[(int64_t)k * d + j] = (float)m;
-    new_var[(int64_t)k * d + j] = (float)(v < 1e-6 ? 1e-6 : v);
-  }
+  for (int j = threadIdx.x; j < d; j += blockDim.x)
+    update_component(nk, s[j], q[j], n_total, floors, new_mu + (int64_t)k * d + j,
+                     new_var + (int64_t)k * d + j);
   if (threadIdx.x == 0)
     new_log_pi[k] = (float)(floors ? log(fmax(nk / n_total, 1e-8)) : log(nk / n_total));
 }

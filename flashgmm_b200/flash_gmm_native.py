@@ -210,6 +210,31 @@ def em_stats(X, mu, var, log_pi, points=None, workspace=None):
     return workspace.stats, workspace.ln
 
 
+def em_step(X, mu, var, log_pi, points=None, workspace=None, out=None):
+    """One EM iteration over prepared points: :func:`em_stats` and :func:`em_update` in
+    one call (the update runs inside the statistics reduction's launch).  Returns
+    ``(new_mu, new_var, new_log_pi, stats, log_normalizer)``; ``out`` may be the input
+    parameter tensors themselves (in-place update)."""
+    X, mu, var, log_pi, N, d, K = _check_params(X, mu, var, log_pi)
+    lib = _lib.load()
+    dev = X.device
+    with torch.cuda.device(dev):
+        if workspace is None or workspace.key != (N, d, K, dev):
+            workspace = StatsWorkspace(N, d, K, dev)
+        if points is None and lib.fgmm_points_bytes(N, d, K) > 0:
+            points = prepare_points(X, K)
+        if out is None:
+            out = (torch.empty(K, d, dtype=torch.float32, device=dev),
+                   torch.empty(K, d, dtype=torch.float32, device=dev),
+                   torch.empty(K, dtype=torch.float32, device=dev))
+        _lib.check(lib.fgmm_em_step(X.data_ptr(), points.data_ptr() if points is not None else None,
+                                    N, d, mu.data_ptr(), var.data_ptr(), log_pi.data_ptr(), K,
+                                    out[0].data_ptr(), out[1].data_ptr(), out[2].data_ptr(),
+                                    workspace.stats.data_ptr(), workspace.ln.data_ptr(),
+                                    workspace.ws.data_ptr(), workspace.ws.numel(), _stream_ptr(dev)))
+    return out[0], out[1], out[2], workspace.stats, workspace.ln
+
+
 def em_update(stats, n_total, K, d, out=None):
     """M-step from (summed) stats -> ``(new_mu, new_var, new_log_pi)``."""
     if stats.dtype != torch.float64 or not stats.is_cuda or stats.numel() != stats_len(K, d):

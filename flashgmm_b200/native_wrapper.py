@@ -140,9 +140,8 @@ class NativeFlashGMM(_EMModel):
         history = []
         for it in range(self.max_iter):
             t0 = time.time()
-            stats, log_norm = _C.em_stats(X, self.mu, self.var, self.log_pi, points=points,
-                                          workspace=ws)
-            self.mu, self.var, self.log_pi = _C.em_update(stats, N, self.K, self.d)
+            self.mu, self.var, self.log_pi, stats, log_norm = _C.em_step(
+                X, self.mu, self.var, self.log_pi, points=points, workspace=ws)
             avg_ll = stats[-1].item() / N
             self.log_normalizer = log_norm
             elapsed = time.time() - t0
@@ -172,8 +171,8 @@ class NativeFlashGMM(_EMModel):
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, stream=stream):
                 for i in range(G):
-                    stats, log_norm = _C.em_stats(X, mu, var, lp, points=points, workspace=ws)
-                    _C.em_update(stats, N, K, d, out=(mu, var, lp))
+                    _, _, _, stats, log_norm = _C.em_step(X, mu, var, lp, points=points,
+                                                          workspace=ws, out=(mu, var, lp))
                     h_ll[i].copy_(stats[-1])
                     h_mu[i].copy_(mu)
                     h_var[i].copy_(var)

@@ -83,6 +83,19 @@ int fgmm_em_stats(const float *X, const void *points, int64_t N, int32_t d,
 int fgmm_em_update(const double *stats, double n_total, int32_t K, int32_t d,
                    float *new_mu, float *new_var, float *new_log_pi, void *stream);
 
+/* One EM iteration on one device over prepared points: fgmm_em_stats followed by
+ * the M-step of fgmm_em_update (n_total = N), the update applied inside the
+ * statistics reduction's launch.  `stats` and `log_normalizer` are written as by
+ * fgmm_em_stats (the log-likelihood is stats[K(2d+1)] / N); the new parameters may
+ * alias mu / var / log_pi.  Replaces one pass of the reference's fit loop
+ * (flash_gmm/native_wrapper.py:128-146 calling flash_em_fused on the same X every
+ * iteration), without re-preparing the point operands. */
+int fgmm_em_step(const float *X, const void *points, int64_t N, int32_t d,
+                 const float *mu, const float *var, const float *log_pi, int32_t K,
+                 float *new_mu, float *new_var, float *new_log_pi,
+                 double *stats, float *log_normalizer,
+                 void *workspace, size_t workspace_bytes, void *stream);
+
 /* One fused EM iteration on one device: stats + update.  The drop-in for the
  * reference's op `flash_em_fused(X, mu, var, log_pi, BN, BK)`
  * (flash_gmm/csrc/binding.cpp:62-76 dispatching to flash_em_fused_cuda,

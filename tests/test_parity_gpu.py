@@ -134,6 +134,25 @@ def test_split_stats_update_equals_fused(family):
     assert abs(stats[-1].item() - ln.double().sum().item()) < 1e-6 * X.shape[0]
 
 
+def test_em_step_equals_split(family):
+    """em_step (update fused into the reduction) == em_stats + em_update, also in place."""
+    from flashgmm_b200 import flash_gmm_native as C
+    g = load_golden("c2_slice2048")
+    dev = torch.device("cuda:0")
+    X, mu, var, lp = (torch.from_numpy(g[k]).to(dev) for k in ("X", "mu", "var", "log_pi"))
+    stats, ln = C.em_stats(X, mu, var, lp)
+    stats, ln = stats.clone(), ln.clone()
+    upd = C.em_update(stats, X.shape[0], mu.shape[0], mu.shape[1])
+    nm, nv, nl, st2, ln2 = C.em_step(X, mu, var, lp)
+    for a, b in zip((nm, nv, nl), upd):
+        assert torch.equal(a, b)
+    assert torch.equal(st2, stats) and torch.equal(ln2, ln)
+    m2, v2, l2 = mu.clone(), var.clone(), lp.clone()
+    C.em_step(X, m2, v2, l2, out=(m2, v2, l2))
+    for a, b in zip((m2, v2, l2), upd):
+        assert torch.equal(a, b)
+
+
 def test_sharded_stats_sum_equals_whole(family):
     """Stats of two halves summed == stats of the whole (the allreduce invariant)."""
     from flashgmm_b200 import flash_gmm_native as C
