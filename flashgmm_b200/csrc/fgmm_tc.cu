@@ -344,18 +344,16 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
       const int64_t n_row = (int64_t)pt * BM + row;
       for (int t = g * tpg; t < t1 && ok; ++t) {
         const int kb = t * NC + part * kPart;
-        // this warp's 32 log-coefficients: one load per lane, issued before the drains and
-        // handed out by shuffles
-        const float cv = __ldg(cst2 + kb + lane);
         float acc[kPart];
         ok = drain_group<NB, true>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
 #pragma unroll 1
         for (int grp = 1; grp < NKC / group_chunks<NKC>() && ok; ++grp)
           ok = drain_group<NB, false>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
         if (!ok) break;
-        float cst[kPart];
+        float cst[kPart];  // this warp's 32 log-coefficients (uniform loads, L1-resident)
 #pragma unroll
-        for (int e = 0; e < kPart; ++e) cst[e] = __shfl_sync(0xffffffffu, cv, e);
+        for (int e = 0; e < kPart; e += 4)
+          *reinterpret_cast<float4 *>(cst + e) = __ldg(reinterpret_cast<const float4 *>(cst2 + kb + e));
         float c4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
 #pragma unroll
         for (int e = 0; e < kPart; ++e) {
@@ -377,14 +375,32 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
         for (int e = 0; e < kPart; ++e) a4[e & 3] += ex2(acc[e] - mr);
         s = (a4[0] + a4[1]) + (a4[2] + a4[3]);
         m = mn;
-        if (cm > v2) {  // rare once the row's leading components are known
+        if (cm > v2) {  // the tile's two largest, without data-dependent branches
+          int e1 = kPart;  // first column at the maximum
+#pragma unroll
+          for (int e = kPart - 1; e >= 0; --e) e1 = acc[e] == cm ? e : e1;
+          float t4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+          int k4[4] = {-1, -1, -1, -1};
 #pragma unroll
           for (int e = 0; e < kPart; ++e) {
-            const float x = acc[e];
+            const bool take = e != e1 && acc[e] > t4[e & 3];
+            t4[e & 3] = take ? acc[e] : t4[e & 3];
+            k4[e & 3] = take ? e : k4[e & 3];
+          }
+          float t2 = t4[0];
+          int e2 = k4[0];
+#pragma unroll
+          for (int c = 1; c < 4; ++c)
+            if (t4[c] > t2 || (t4[c] == t2 && k4[c] >= 0 && (e2 < 0 || k4[c] < e2))) { t2 = t4[c]; e2 = k4[c]; }
+          auto insert = [&](float x, int ix) {
             if (x > v2) {
-              if (x > v1) { v2 = v1; i2 = i1; v1 = x; i1 = kb + e; }
-              else        { v2 = x; i2 = kb + e; }
+              if (x > v1) { v2 = v1; i2 = i1; v1 = x; i1 = ix; }
+              else        { v2 = x; i2 = ix; }
             }
+          };
+          if (e1 < kPart) {
+            insert(cm, kb + e1);
+            if (e2 >= 0) insert(t2, kb + e2);
           }
         }
       }
@@ -448,8 +464,11 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
 // block.
 // Eight lanes per point (four points per warp), lanes striped over the dimensions; all
 // loads of a point are issued before its reductions.
+#ifndef FGMM_REFINE_MINB
+#define FGMM_REFINE_MINB 4
+#endif
 template <int DPL, bool VEC>  // dimensions per lane: ceil(d / 8); VEC: float4 loads
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, FGMM_REFINE_MINB)
 tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__restrict__ sc,
                  const float *__restrict__ ms, const float *__restrict__ lc,
                  const float *__restrict__ part_m, const float *__restrict__ part_s,
@@ -467,12 +486,36 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
        n += stride) {
     const bool live = n < N;
     const int64_t nn = live ? n : 0;
-    float mx = -INFINITY, b1 = -INFINITY, b2 = -INFINITY;
+    // the point's row first (independent of everything below), so its latency overlaps
+    // the partial loads and the parameter gathers
+    float x[DPL], s1[DPL], m1[DPL], s2[DPL], m2[DPL];
+    if (VEC) {  // d == 8 DPL, DPL % 4 == 0, 16-byte aligned rows; lane takes float4 i * 8 + sub
+      const float4 *xp = reinterpret_cast<const float4 *>(X + nn * d) + sub;
+#pragma unroll
+      for (int i = 0; i < DPL / 4; ++i) {
+        const float4 a = __ldg(xp + 8 * i);
+        x[4 * i] = a.x; x[4 * i + 1] = a.y; x[4 * i + 2] = a.z; x[4 * i + 3] = a.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) {
+        const int j = i * 8 + sub;
+        x[i] = j < d ? __ldg(X + nn * d + j) : 0.0f;
+      }
+    }
+    // merge the component groups' partials: online log-sum-exp and top-2
+    float mx = -INFINITY, sm = 0.0f, b1 = -INFINITY, b2 = -INFINITY;
     int j1 = -1, j2 = -1;
+#pragma unroll 4
     for (int g = 0; g < G; ++g) {
-      mx = fmaxf(mx, __ldg(part_m + (int64_t)g * N + nn));
+      const float pm = __ldg(part_m + (int64_t)g * N + nn);
+      const float ps = __ldg(part_s + (int64_t)g * N + nn);
       const float2 tv = part_tv[(int64_t)g * N + nn];
       const int2 ti = part_ti[(int64_t)g * N + nn];
+      const float mn = fmaxf(mx, pm);
+      const float mr = mn == -INFINITY ? 0.0f : mn;
+      sm = sm * ex2(mx - mr) + ps * ex2(pm - mr);
+      mx = mn;
       if (ti.x >= 0 && tv.x > b2) {
         if (tv.x > b1) { b2 = b1; j2 = j1; b1 = tv.x; j1 = ti.x; }
         else           { b2 = tv.x; j2 = ti.x; }
@@ -482,9 +525,6 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
         else           { b2 = tv.y; j2 = ti.y; }
       }
     }
-    float sm = 0.0f;
-    for (int g = 0; g < G; ++g)
-      sm += __ldg(part_s + (int64_t)g * N + nn) * ex2(__ldg(part_m + (int64_t)g * N + nn) - mx);
     // the runner-up only matters when it is within 2^-40 of the leader (otherwise its
     // responsibility is below 1e-12 and its tensor-core value is kept)
     if (j2 >= 0 && b2 < b1 - 40.0f) j2 = -1;
@@ -492,20 +532,17 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
     const bool need2 = __any_sync(0xffffffffu, j2 >= 0);
     // the 8 lanes of a point read each row in consecutive 16-byte (VEC) or 4-byte pieces,
     // so a load instruction of the warp touches whole 128-byte lines
-    float x[DPL], s1[DPL], m1[DPL], s2[DPL], m2[DPL];
     const bool use2 = need2 && j2 >= 0;
-    if (VEC) {  // d == 8 DPL, DPL % 4 == 0, 16-byte aligned rows; lane takes float4 i * 8 + sub
-      const float4 *xp = reinterpret_cast<const float4 *>(X + nn * d) + sub;
+    if (VEC) {
       const float4 *s1p = reinterpret_cast<const float4 *>(sc + (int64_t)k1 * d) + sub;
       const float4 *m1p = reinterpret_cast<const float4 *>(ms + (int64_t)k1 * d) + sub;
       const float4 *s2p = reinterpret_cast<const float4 *>(sc + (int64_t)k2 * d) + sub;
       const float4 *m2p = reinterpret_cast<const float4 *>(ms + (int64_t)k2 * d) + sub;
 #pragma unroll
       for (int i = 0; i < DPL / 4; ++i) {
-        const float4 a = __ldg(xp + 8 * i), b = __ldg(s1p + 8 * i), c = __ldg(m1p + 8 * i);
+        const float4 b = __ldg(s1p + 8 * i), c = __ldg(m1p + 8 * i);
         const float4 e = use2 ? __ldg(s2p + 8 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
         const float4 f = use2 ? __ldg(m2p + 8 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
-        x[4 * i] = a.x; x[4 * i + 1] = a.y; x[4 * i + 2] = a.z; x[4 * i + 3] = a.w;
         s1[4 * i] = b.x; s1[4 * i + 1] = b.y; s1[4 * i + 2] = b.z; s1[4 * i + 3] = b.w;
         m1[4 * i] = c.x; m1[4 * i + 1] = c.y; m1[4 * i + 2] = c.z; m1[4 * i + 3] = c.w;
         s2[4 * i] = e.x; s2[4 * i + 1] = e.y; s2[4 * i + 2] = e.z; s2[4 * i + 3] = e.w;
@@ -516,7 +553,6 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
       for (int i = 0; i < DPL; ++i) {
         const int j = i * 8 + sub;
         const bool in = j < d;
-        x[i] = in ? __ldg(X + nn * d + j) : 0.0f;
         s1[i] = in ? __ldg(sc + (int64_t)k1 * d + j) : 0.0f;
         m1[i] = in ? __ldg(ms + (int64_t)k1 * d + j) : 0.0f;
         s2[i] = in && use2 ? __ldg(sc + (int64_t)k2 * d + j) : 0.0f;

@@ -18,7 +18,10 @@ namespace fgmm {
 // fixed order (deterministic) in fp64.  With `up`, the same block then applies the
 // M-step to its component (em_update_kernel's arithmetic), which saves the update launch.
 constexpr int kRedThreads = 512;
-constexpr int kRedBatch = 8;
+#ifndef FGMM_RED_BATCH
+#define FGMM_RED_BATCH 8
+#endif
+constexpr int kRedBatch = FGMM_RED_BATCH;
 struct UpdateArgs {
   double n_total;
   float *mu, *var, *log_pi;
