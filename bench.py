@@ -398,7 +398,7 @@ def run_e2e(wl, dev, args, ws_n=1, rank=0, steps=200):
     ph = [t.pin_memory() for t in (mu, var, lp)]
     N, d, K = wl.N, wl.d, wl.K
     Xd = [torch.empty_like(X, device=dev) for _ in range(2)]
-    pd = [torch.empty_like(t, device=dev) for t in ph]
+    pd = [[torch.empty_like(t, device=dev) for t in ph] for _ in range(2)]
     out_h = [torch.empty_like(t).pin_memory() for t in ph] + [torch.empty(N).pin_memory()]
     copy = torch.cuda.Stream(dev)
     comp = torch.cuda.current_stream(dev)
@@ -407,23 +407,26 @@ def run_e2e(wl, dev, args, ws_n=1, rank=0, steps=200):
     ws = C.StatsWorkspace(N, d, K, dev) if ws_n > 1 else None
 
     def issue_copy(i):
+        # all host-to-device traffic of step i on the copy stream (a small copy queued on
+        # the compute stream would wait behind the next step's X copy in the copy engine)
         b = i % 2
         with torch.cuda.stream(copy):
             copy.wait_event(freed[b])
+            for t, h in zip(pd[b], ph):
+                t.copy_(h, non_blocking=True)
             Xd[b].copy_(Xh, non_blocking=True)
             landed[b].record(copy)
 
     def step(i):
         b = i % 2
         comp.wait_event(landed[b])
-        for t, h in zip(pd, ph):
-            t.copy_(h, non_blocking=True)
+        mu_d, var_d, lp_d = pd[b]
         if ws_n > 1:
-            stats, ln = C.em_stats(Xd[b], pd[0], pd[1], pd[2], workspace=ws)
+            stats, ln = C.em_stats(Xd[b], mu_d, var_d, lp_d, workspace=ws)
             dist.all_reduce(stats)
             out = list(C.em_update(stats, n_total, K, d)) + [ln]
         else:
-            out = C.flash_em_fused(Xd[b], pd[0], pd[1], pd[2])
+            out = C.flash_em_fused(Xd[b], mu_d, var_d, lp_d)
         freed[b].record(comp)
         for h, t in zip(out_h, out):
             h.copy_(t, non_blocking=True)
