@@ -110,6 +110,85 @@ reduce_partials_kernel(const float *__restrict__ part, int slots, int K, int d, 
   }
 }
 
+// The same reduction for rows whose statistics runs are 16-byte aligned (ds and W
+// multiples of 4, as the tensor-core family writes them): warp w of the block sums slots
+// w, w + 16, ... with float4 loads (lane: four consecutive dimensions), four slots' loads
+// in flight per lane, and the 16 warp sums are added in a fixed order.
+constexpr int kRed4Warps = 16;
+__global__ void __launch_bounds__(32 * kRed4Warps)
+reduce_rows4_kernel(const float *__restrict__ part, int slots, int K, int d, int ds, int W,
+                    const double *__restrict__ lnp, int ln_slots, double *__restrict__ stats,
+                    UpdateArgs up) {
+  __shared__ double sh_s[kRed4Warps][128], sh_q[kRed4Warps][128];
+  __shared__ double sh_n[kRed4Warps];
+  griddep_launch();
+  griddep_wait();
+  const int k = blockIdx.x, t = threadIdx.x, lane = t & 31, w = t >> 5;
+  if (k == K) {  // the log-normalizer sum
+    double a = 0.0;
+    for (int j = t; j < ln_slots; j += 32 * kRed4Warps) a += lnp[j];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    if (lane == 0) sh_n[w] = a;
+    __syncthreads();
+    if (t == 0) {
+      double tot = 0.0;
+      for (int u = 0; u < kRed4Warps; ++u) tot += sh_n[u];
+      stats[K + 2 * (int64_t)K * d] = tot;
+    }
+    return;
+  }
+  const float *pk = part + (int64_t)k * slots * W;
+  double nk = 0.0;
+  for (int j0 = 0; j0 < d; j0 += 128) {
+    const int j = j0 + 4 * lane;
+    const bool in = j < d;
+    double as[4] = {0.0, 0.0, 0.0, 0.0}, aq[4] = {0.0, 0.0, 0.0, 0.0}, an = 0.0;
+    for (int sl = w; sl < slots; sl += 4 * kRed4Warps) {
+      float4 vs[4], vq[4];
+      float vn[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int su = sl + u * kRed4Warps;
+        const bool live = su < slots;
+        const float *row = pk + (int64_t)(live ? su : 0) * W;
+        vs[u] = live && in ? __ldg(reinterpret_cast<const float4 *>(row + j)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        vq[u] = live && in ? __ldg(reinterpret_cast<const float4 *>(row + ds + j)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        vn[u] = live && j0 == 0 && lane == 0 ? __ldg(row + 2 * ds) : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        as[0] += (double)vs[u].x; as[1] += (double)vs[u].y; as[2] += (double)vs[u].z; as[3] += (double)vs[u].w;
+        aq[0] += (double)vq[u].x; aq[1] += (double)vq[u].y; aq[2] += (double)vq[u].z; aq[3] += (double)vq[u].w;
+        an += (double)vn[u];
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) { sh_s[w][4 * lane + e] = as[e]; sh_q[w][4 * lane + e] = aq[e]; }
+    if (j0 == 0 && lane == 0) sh_n[w] = an;
+    __syncthreads();
+    if (j0 == 0) {
+      for (int u = 0; u < kRed4Warps; ++u) nk += sh_n[u];  // every thread, same order
+    }
+    if (t < 128 && j0 + t < d) {
+      double sv = 0.0, qv = 0.0;
+      for (int u = 0; u < kRed4Warps; ++u) { sv += sh_s[u][t]; qv += sh_q[u][t]; }
+      const int jj = j0 + t;
+      stats[K + (int64_t)k * d + jj] = sv;
+      stats[K + (int64_t)K * d + (int64_t)k * d + jj] = qv;
+      if (up.on)
+        update_component(nk, sv, qv, up.n_total, up.floors, up.mu + (int64_t)k * d + jj,
+                         up.var + (int64_t)k * d + jj);
+    }
+    __syncthreads();
+  }
+  if (t == 0) {
+    stats[k] = nk;
+    if (up.on)
+      up.log_pi[k] = (float)(up.floors ? log(fmax(nk / up.n_total, 1e-8)) : log(nk / up.n_total));
+  }
+}
+
 int reduce_partials(const float *partials, int slots, int K, int d, int ds, int W,
                     const double *ln_partials, int ln_slots, double *stats, cudaStream_t stream,
                     const UpdateOut *update) {
@@ -122,8 +201,15 @@ int reduce_partials(const float *partials, int slots, int K, int d, int ds, int 
     up.floors = update->floors ? 1 : 0;
     up.on = 1;
   }
-  FGMM_CUDA_TRY(launch_pdl(reduce_partials_kernel, K + 1, kRedThreads, 0, stream, partials, slots,
-                           K, d, ds, W, ln_partials, ln_slots, stats, up));
+#ifndef FGMM_RED_ROWS4
+#define FGMM_RED_ROWS4 1
+#endif
+  if (FGMM_RED_ROWS4 && ds % 4 == 0 && W % 4 == 0 && reinterpret_cast<uintptr_t>(partials) % 16 == 0)
+    FGMM_CUDA_TRY(launch_pdl(reduce_rows4_kernel, K + 1, 32 * kRed4Warps, 0, stream, partials,
+                             slots, K, d, ds, W, ln_partials, ln_slots, stats, up));
+  else
+    FGMM_CUDA_TRY(launch_pdl(reduce_partials_kernel, K + 1, kRedThreads, 0, stream, partials,
+                             slots, K, d, ds, W, ln_partials, ln_slots, stats, up));
   mark(stream, "reduce_partials_kernel");
   return FGMM_OK;
 }
