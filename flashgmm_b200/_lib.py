@@ -32,7 +32,7 @@ SIGNATURES = {
     "fgmm_em_stats": (ctypes.c_int, [_vp, _vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _sz, _vp]),
     "fgmm_em_update": (ctypes.c_int, [_vp, _d, _i32, _i32, _vp, _vp, _vp, _vp]),
     "fgmm_em_step": (ctypes.c_int, [_vp, _vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp,
-                                    _vp, _sz, _vp]),
+                                    _vp, _sz, _i32, _vp]),
     "fgmm_device_error": (ctypes.c_int, [ctypes.c_int]),
     "fgmm_em_stats_launches": (ctypes.c_int, [_i64, _i32, _i32]),
     "fgmm_em_stats_profiled": (ctypes.c_int, [_vp, _vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _sz, _vp,

@@ -104,7 +104,7 @@ namespace {
 int em_stats_impl(const float *X, const void *points, int64_t N, int32_t d, const float *mu,
                   const float *var, const float *log_pi, int32_t K, double *stats,
                   float *log_normalizer, void *workspace, size_t workspace_bytes, void *stream,
-                  const fgmm::UpdateOut *update) {
+                  const fgmm::UpdateOut *update, bool prepared = false) {
   int rc = check_shape(N, d, K);
   if (rc) return rc;
   if (!X || !mu || !var || !log_pi || !stats || !log_normalizer || !workspace)
@@ -132,7 +132,8 @@ int em_stats_impl(const float *X, const void *points, int64_t N, int32_t d, cons
   } else if (workspace_bytes < need) {
     return fail(FGMM_ERR_WORKSPACE, "workspace too small");
   }
-  return tc_em_stats(X, pts, N, d, mu, var, log_pi, K, stats, log_normalizer, workspace, st, update);
+  return tc_em_stats(X, pts, N, d, mu, var, log_pi, K, stats, log_normalizer, workspace, st, update,
+                     prepared);
 }
 }  // namespace
 
@@ -146,11 +147,20 @@ int fgmm_em_stats(const float *X, const void *points, int64_t N, int32_t d, cons
 int fgmm_em_step(const float *X, const void *points, int64_t N, int32_t d, const float *mu,
                  const float *var, const float *log_pi, int32_t K, float *new_mu, float *new_var,
                  float *new_log_pi, double *stats, float *log_normalizer, void *workspace,
-                 size_t workspace_bytes, void *stream) {
+                 size_t workspace_bytes, int32_t flags, void *stream) {
   if (!new_mu || !new_var || !new_log_pi) return fail(FGMM_ERR_INVALID, "null pointer argument");
-  const fgmm::UpdateOut up{(double)N, new_mu, new_var, new_log_pi, true};
+  if (flags & ~FGMM_STEP_PREPARED) return fail(FGMM_ERR_INVALID, "unknown flags");
+  const bool prepared = (flags & FGMM_STEP_PREPARED) != 0;
+  if (prepared && (!points || resolve_family(N, d, K) != FGMM_FAMILY_TC))
+    return fail(FGMM_ERR_INVALID, "FGMM_STEP_PREPARED needs the tensor-core family and prepared points");
+  fgmm::UpdateOut up{};
+  up.n_total = (double)N;
+  up.mu = new_mu;
+  up.var = new_var;
+  up.log_pi = new_log_pi;
+  up.floors = true;
   return em_stats_impl(X, points, N, d, mu, var, log_pi, K, stats, log_normalizer, workspace,
-                       workspace_bytes, stream, &up);
+                       workspace_bytes, stream, &up, prepared);
 }
 
 int fgmm_em_update(const double *stats, double n_total, int32_t K, int32_t d, float *new_mu,

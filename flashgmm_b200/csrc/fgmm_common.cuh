@@ -98,6 +98,11 @@ struct UpdateOut {
   double n_total;
   float *mu, *var, *log_pi;
   bool floors;
+  // Optional (tensor-core family, d <= 128): also write the next iteration's pass-1
+  // operands for the updated parameters, as tc_prep_params_kernel would (dp = 0: off).
+  float *qhi = nullptr, *qlo = nullptr, *cst2 = nullptr, *sc = nullptr, *ms = nullptr,
+        *lc = nullptr;
+  int dp = 0;
 };
 
 // ---- SIMT family (fgmm_simt.cu) ----
@@ -115,7 +120,8 @@ int tc_prepare_points(const float *X, int64_t N, int d, void *points, cudaStream
 int tc_device_error(bool reset);
 int tc_em_stats(const float *X, const void *points, int64_t N, int d, const float *mu,
                 const float *var, const float *log_pi, int K, double *stats,
-                float *log_norm, void *ws, cudaStream_t stream, const UpdateOut *update = nullptr);
+                float *log_norm, void *ws, cudaStream_t stream, const UpdateOut *update = nullptr,
+                bool prepared = false);
 
 // ---- shared epilogue kernels (fgmm_update.cu) ----
 // Sums per-block fp32 partials [K][slots][W] (rows [s (ds) | sq (ds) | n ...]) and

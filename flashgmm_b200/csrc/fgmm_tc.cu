@@ -1152,12 +1152,22 @@ int tc_prepare_points(const float *X, int64_t N, int d, void *points, cudaStream
 
 int tc_em_stats(const float *X, const void *points, int64_t N, int d, const float *mu,
                 const float *var, const float *log_pi, int K, double *stats, float *log_norm,
-                void *ws, cudaStream_t st, const UpdateOut *update) {
+                void *ws, cudaStream_t st, const UpdateOut *update, bool prepared) {
   const TcPlan p = plan(N, d, K);
   const TcWs w = tc_layout(ws, p);
-  FGMM_CUDA_TRY(launch_pdl(tc_prep_params_kernel, p.Kp, 128, 0, st, mu, var, log_pi, K, d, p.dp,
-                           w.qhi, w.qlo, w.cst2, w.sc, w.ms, w.lc));
-  mark(st, "tc_prep_params_kernel");
+  // `prepared`: the workspace already holds the operands of (mu, var, log_pi), written by
+  // the previous call's fused update
+  if (!prepared) {
+    FGMM_CUDA_TRY(launch_pdl(tc_prep_params_kernel, p.Kp, 128, 0, st, mu, var, log_pi, K, d, p.dp,
+                             w.qhi, w.qlo, w.cst2, w.sc, w.ms, w.lc));
+    mark(st, "tc_prep_params_kernel");
+  }
+  UpdateOut up{};
+  if (update) {  // the update also prepares the next iteration's operands
+    up = *update;
+    up.qhi = w.qhi; up.qlo = w.qlo; up.cst2 = w.cst2; up.sc = w.sc; up.ms = w.ms; up.lc = w.lc;
+    up.dp = p.dp;
+  }
   const float *pts = static_cast<const float *>(points);
   int rc;
   switch (p.nkc) {
@@ -1169,7 +1179,7 @@ int tc_em_stats(const float *X, const void *points, int64_t N, int d, const floa
   }
   if (rc) return rc;
   return reduce_partials(w.partial, p.first.S, K, d, p.dp, 2 * p.dp + 4, w.ln_part,
-                         refine_blocks(p.first.Nc), stats, st, update);
+                         refine_blocks(p.first.Nc), stats, st, update ? &up : nullptr);
 }
 
 int tc_device_error(bool reset) {

@@ -210,11 +210,17 @@ def em_stats(X, mu, var, log_pi, points=None, workspace=None):
     return workspace.stats, workspace.ln
 
 
-def em_step(X, mu, var, log_pi, points=None, workspace=None, out=None):
+STEP_PREPARED = 1
+
+
+def em_step(X, mu, var, log_pi, points=None, workspace=None, out=None, prepared=False):
     """One EM iteration over prepared points: :func:`em_stats` and :func:`em_update` in
     one call (the update runs inside the statistics reduction's launch).  Returns
     ``(new_mu, new_var, new_log_pi, stats, log_normalizer)``; ``out`` may be the input
-    parameter tensors themselves (in-place update)."""
+    parameter tensors themselves (in-place update).  ``prepared=True`` asserts that
+    ``mu, var, log_pi`` are exactly the outputs of the previous ``em_step`` with this
+    ``workspace`` (and ``points``), so their tensor-core operands, which that call left
+    in the workspace, are reused instead of rebuilt."""
     X, mu, var, log_pi, N, d, K = _check_params(X, mu, var, log_pi)
     lib = _lib.load()
     dev = X.device
@@ -231,7 +237,8 @@ def em_step(X, mu, var, log_pi, points=None, workspace=None, out=None):
                                     N, d, mu.data_ptr(), var.data_ptr(), log_pi.data_ptr(), K,
                                     out[0].data_ptr(), out[1].data_ptr(), out[2].data_ptr(),
                                     workspace.stats.data_ptr(), workspace.ln.data_ptr(),
-                                    workspace.ws.data_ptr(), workspace.ws.numel(), _stream_ptr(dev)))
+                                    workspace.ws.data_ptr(), workspace.ws.numel(),
+                                    STEP_PREPARED if prepared else 0, _stream_ptr(dev)))
     return out[0], out[1], out[2], workspace.stats, workspace.ln
 
 

@@ -134,14 +134,19 @@ class NativeFlashGMM(_EMModel):
         N = X.shape[0]
         points = _C.prepare_points(X, self.K)
         ws = _C.StatsWorkspace(N, self.d, self.K, X.device)
+        # the tensor-core family reuses the operands each step leaves for the next one
+        self._reuse = _C.family_for(N, self.d, self.K) == 2
         if graph_iters and graph_iters > 1 and self.max_iter > 1:
             return self._fit_graph(X, N, points, ws, verbose, int(graph_iters))
         prev_ll = -float("inf")
         history = []
         for it in range(self.max_iter):
             t0 = time.time()
+            # from the second iteration on, the parameters are the previous step's outputs,
+            # whose tensor-core operands that step already left in the workspace
             self.mu, self.var, self.log_pi, stats, log_norm = _C.em_step(
-                X, self.mu, self.var, self.log_pi, points=points, workspace=ws)
+                X, self.mu, self.var, self.log_pi, points=points, workspace=ws,
+                prepared=self._reuse and it > 0)
             avg_ll = stats[-1].item() / N
             self.log_normalizer = log_norm
             elapsed = time.time() - t0
@@ -172,7 +177,8 @@ class NativeFlashGMM(_EMModel):
             with torch.cuda.graph(graph, stream=stream):
                 for i in range(G):
                     _, _, _, stats, log_norm = _C.em_step(X, mu, var, lp, points=points,
-                                                          workspace=ws, out=(mu, var, lp))
+                                                          workspace=ws, out=(mu, var, lp),
+                                                          prepared=self._reuse and i > 0)
                     h_ll[i].copy_(stats[-1])
                     h_mu[i].copy_(mu)
                     h_var[i].copy_(var)

@@ -87,14 +87,20 @@ int fgmm_em_update(const double *stats, double n_total, int32_t K, int32_t d,
  * the M-step of fgmm_em_update (n_total = N), the update applied inside the
  * statistics reduction's launch.  `stats` and `log_normalizer` are written as by
  * fgmm_em_stats (the log-likelihood is stats[K(2d+1)] / N); the new parameters may
- * alias mu / var / log_pi.  Replaces one pass of the reference's fit loop
- * (flash_gmm/native_wrapper.py:128-146 calling flash_em_fused on the same X every
- * iteration), without re-preparing the point operands. */
+ * alias mu / var / log_pi.  The same launch also leaves in `workspace` the
+ * tensor-core operands of the new parameters: a following call whose mu / var /
+ * log_pi are exactly this call's outputs (unchanged in between) and whose workspace
+ * is the same may pass FGMM_STEP_PREPARED in `flags` to skip preparing them again
+ * (tensor-core family with prepared points only; otherwise FGMM_ERR_INVALID).
+ * Replaces one pass of the reference's fit loop (flash_gmm/native_wrapper.py:128-146
+ * calling flash_em_fused on the same X every iteration), without re-preparing the
+ * point operands. */
+#define FGMM_STEP_PREPARED 1
 int fgmm_em_step(const float *X, const void *points, int64_t N, int32_t d,
                  const float *mu, const float *var, const float *log_pi, int32_t K,
                  float *new_mu, float *new_var, float *new_log_pi,
                  double *stats, float *log_normalizer,
-                 void *workspace, size_t workspace_bytes, void *stream);
+                 void *workspace, size_t workspace_bytes, int32_t flags, void *stream);
 
 /* One fused EM iteration on one device: stats + update.  The drop-in for the
  * reference's op `flash_em_fused(X, mu, var, log_pi, BN, BK)`

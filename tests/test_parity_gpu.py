@@ -153,6 +153,26 @@ def test_em_step_equals_split(family):
         assert torch.equal(a, b)
 
 
+def test_em_step_prepared_operands(family):
+    """A step that reuses the operands the previous step's fused update left in the
+    workspace (prepared=True) == the same step preparing them itself."""
+    from flashgmm_b200 import flash_gmm_native as C
+    if C.family_for(2048, 128, 256) != 2:
+        pytest.skip("operand reuse is a tensor-core family feature")
+    g = load_golden("c2_slice2048")
+    dev = torch.device("cuda:0")
+    X, mu, var, lp = (torch.from_numpy(g[k]).to(dev) for k in ("X", "mu", "var", "log_pi"))
+    N, d, K = X.shape[0], X.shape[1], mu.shape[0]
+    pts = C.prepare_points(X, K)
+    ws = C.StatsWorkspace(N, d, K, dev)
+    p1 = [t.clone() for t in C.em_step(X, mu, var, lp, points=pts, workspace=ws)[:3]]
+    a = [t.clone() for t in C.em_step(X, *p1, points=pts, workspace=ws, prepared=True)]
+    ws2 = C.StatsWorkspace(N, d, K, dev)
+    b = [t.clone() for t in C.em_step(X, *p1, points=pts, workspace=ws2, prepared=False)]
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
+
+
 def test_sharded_stats_sum_equals_whole(family):
     """Stats of two halves summed == stats of the whole (the allreduce invariant)."""
     from flashgmm_b200 import flash_gmm_native as C
