@@ -176,30 +176,27 @@ __host__ __device__ constexpr int group_chunks() {
 
 // MMA side: one staged 32-column chunk of a K group that rotates over NB TMEM buffers;
 // gfirst / glast mark the group's first / last chunk.
+// `desc` is the stage's shared-memory descriptor (SWIZZLE_128B K-major, stage base); the
+// operand tiles and k-steps are fixed offsets of its 16-byte address field, so the issuing
+// thread (which shares its scheduler with a quarter of the epilogue warps) spends one add
+// per operand.
 template <int NB>
-__device__ __forceinline__ bool issue_dist_chunk(uint32_t base, uint32_t tmem, uint32_t &gcount,
+__device__ __forceinline__ bool issue_dist_chunk(uint64_t desc, uint32_t tmem, uint32_t &gcount,
                                                  uint32_t tfull0, uint32_t tempty0, bool gfirst,
                                                  bool glast) {
   constexpr uint32_t idesc = idesc_tf32(BM, NC, 0, 0);
+  constexpr uint64_t kT = kTileBytes >> 4, kK = 32 >> 4;  // tile and k-step offsets
   const uint32_t buf = gcount % NB, use = gcount / NB;
   if (gfirst && !mbar_wait(tempty0 + 8u * buf, (use & 1u) ^ 1u, kErrWaitTmemEmpty)) return false;
   tc_fence_after();
   const uint32_t d = tmem + buf * NC;
 #pragma unroll
   for (int kk = 0; kk < KC / 8; ++kk) {
-    const uint64_t ah = sdesc_sw128(base + kk * 32, 16, 1024);
-    const uint64_t al = sdesc_sw128(base + kTileBytes + kk * 32, 16, 1024);
-    const uint64_t bh = sdesc_sw128(base + 2 * kTileBytes + kk * 32, 16, 1024);
-    const uint64_t bl = sdesc_sw128(base + 3 * kTileBytes + kk * 32, 16, 1024);
-    mma_tf32(d, al, bh, idesc, (kk != 0 || !gfirst) ? 1u : 0u);
-    mma_tf32(d, ah, bl, idesc, 1u);
+    mma_tf32(d, desc + kT + kk * kK, desc + 2 * kT + kk * kK, idesc, (kk != 0 || !gfirst) ? 1u : 0u);
+    mma_tf32(d, desc + kk * kK, desc + 3 * kT + kk * kK, idesc, 1u);
   }
 #pragma unroll
-  for (int kk = 0; kk < KC / 8; ++kk) {
-    const uint64_t ah = sdesc_sw128(base + kk * 32, 16, 1024);
-    const uint64_t bh = sdesc_sw128(base + 2 * kTileBytes + kk * 32, 16, 1024);
-    mma_tf32(d, ah, bh, idesc, 1u);
-  }
+  for (int kk = 0; kk < KC / 8; ++kk) mma_tf32(d, desc + kk * kK, desc + 2 * kT + kk * kK, idesc, 1u);
   if (glast) {
     mma_commit(tfull0 + 8u * buf);
     ++gcount;
@@ -309,6 +306,7 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
       int stage = 0;
       uint32_t phase = 0, gcount = 0;
       bool ok = true;
+      const uint64_t desc0 = sdesc_sw128(smem_u32(smem), 16, 1024);
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
         const int g = u % G;
         const int t1 = min(n_ct, (g + 1) * tpg);
@@ -317,8 +315,11 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
             if (!mbar_wait(FULL(stage), phase, kErrWaitFull)) { ok = false; break; }
             tc_fence_after();
             constexpr int GC = group_chunks<NKC>();
-            if (!issue_dist_chunk<NB>(smem_u32(smem + stage * kStageBytes), tmem, gcount, TFULL0,
-                                      TEMPTY0, c % GC == 0, c % GC == GC - 1)) { ok = false; break; }
+            if (!issue_dist_chunk<NB>(desc0 + (uint64_t)((stage * kStageBytes) >> 4), tmem, gcount,
+                                      TFULL0, TEMPTY0, c % GC == 0, c % GC == GC - 1)) {
+              ok = false;
+              break;
+            }
             mma_commit(EMPTY(stage));
             if (++stage == S) { stage = 0; phase ^= 1; }
           }
@@ -464,11 +465,9 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
 // block.
 // Eight lanes per point (four points per warp), lanes striped over the dimensions; all
 // loads of a point are issued before its reductions.
-#ifndef FGMM_REFINE_MINB
-#define FGMM_REFINE_MINB 4
-#endif
+// Blocks per SM (register budget): five for 16 dimensions per lane, four below (measured).
 template <int DPL, bool VEC>  // dimensions per lane: ceil(d / 8); VEC: float4 loads
-__global__ void __launch_bounds__(256, FGMM_REFINE_MINB)
+__global__ void __launch_bounds__(256, DPL >= 16 ? 5 : 4)
 tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__restrict__ sc,
                  const float *__restrict__ ms, const float *__restrict__ lc,
                  const float *__restrict__ part_m, const float *__restrict__ part_s,
@@ -801,6 +800,7 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
   } else if (warp == kGammaWarps) {
     // ---------------- MMA warp
     constexpr uint32_t idesc = idesc_tf32(NC, KA, 0, 1);  // A from TMEM, B MN-major
+    const uint64_t fdesc0 = sdesc(smem_u32(smem), Sh::kAtom, 512, kSw128Base32);
     for (int s = 0; s < S && ok; ++s) {
       const int j = s / kSlicesFlush, reg = NSR == 2 ? (j & 1) : 0;
       const bool tile_first = s % kSlicesFlush == 0;
@@ -816,19 +816,16 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
         tc_fence_after();
         const uint32_t gbuf = tmem + kGBase + gb * kGCols;
         const uint32_t dst = tmem + reg * KA;
-        const uint32_t base = smem_u32(smem + st * Sh::kStage);
+        // the stage's descriptor; F lo and the second k-step are fixed address offsets
+        const uint64_t fd = fdesc0 + (uint64_t)((st * Sh::kStage) >> 4);
+        constexpr uint64_t kLo = Sh::kFPart >> 4, kK = 1024 >> 4;
 #pragma unroll
         for (int kk = 0; kk < 2; ++kk) {
-          const uint64_t fh = sdesc(base + kk * 1024, Sh::kAtom, 512, kSw128Base32);
-          const uint64_t fl = sdesc(base + Sh::kFPart + kk * 1024, Sh::kAtom, 512, kSw128Base32);
-          mma_tf32_ta(dst, gbuf + kSlicePts + kk * 8, fh, idesc, (tile_first && kk == 0) ? 0u : 1u);
-          mma_tf32_ta(dst, gbuf + kk * 8, fl, idesc, 1u);
+          mma_tf32_ta(dst, gbuf + kSlicePts + kk * 8, fd + kk * kK, idesc, (tile_first && kk == 0) ? 0u : 1u);
+          mma_tf32_ta(dst, gbuf + kk * 8, fd + kLo + kk * kK, idesc, 1u);
         }
 #pragma unroll
-        for (int kk = 0; kk < 2; ++kk) {
-          const uint64_t fh = sdesc(base + kk * 1024, Sh::kAtom, 512, kSw128Base32);
-          mma_tf32_ta(dst, gbuf + kk * 8, fh, idesc, 1u);
-        }
+        for (int kk = 0; kk < 2; ++kk) mma_tf32_ta(dst, gbuf + kk * 8, fd + kk * kK, idesc, 1u);
         mma_commit(EMPTY(st));
         mma_commit(GEMPTY(gb));
         if (s % kSlicesFlush == kSlicesFlush - 1 || s == S - 1) mma_commit(SFULL(reg));
