@@ -380,7 +380,7 @@ def run_ours(args, wl):
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": wl.name, "N_per_gpu": N, "K": K, "d": d,
                        "N_total": n_total, "parallelism": f"dp{ws_n}" if ws_n > 1 else "single",
-                       "family": {1: "simt", 2: "tcgen05"}.get(C.family_for(N, d, K), "?"),
+                       "family": {1: "simt", 2: "tcgen05", 3: "lowk"}.get(C.family_for(N, d, K), "?"),
                        "l2": "flushed between timed iterations (256 MB write, untimed)"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
             "gpu_launches": launches * args.steps,

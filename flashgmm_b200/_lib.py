@@ -16,7 +16,7 @@ FGMM_ERR_INVALID = 1
 FGMM_ERR_UNSUPPORTED = 2
 FGMM_ERR_WORKSPACE = 3
 FGMM_ERR_CUDA = 4
-FAMILY_AUTO, FAMILY_SIMT, FAMILY_TC = 0, 1, 2
+FAMILY_AUTO, FAMILY_SIMT, FAMILY_TC, FAMILY_LOWK = 0, 1, 2, 3
 
 # (name, restype, argtypes) for every symbol the header declares.
 _vp, _i64, _i32, _sz, _d = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_size_t, ctypes.c_double

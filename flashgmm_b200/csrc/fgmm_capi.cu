@@ -51,8 +51,12 @@ static bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_
 static int resolve_family(int64_t N, int d, int K) {
   if (N < 1 || K < 1 || d < 1 || d > 256) return -1;
   const bool tc = tc_supported(N, d, K);
+  const bool lowk = lowk_supported(N, d, K);
   if (g_family == FGMM_FAMILY_SIMT) return FGMM_FAMILY_SIMT;
   if (g_family == FGMM_FAMILY_TC) return tc ? FGMM_FAMILY_TC : -1;
+  if (g_family == FGMM_FAMILY_LOWK) return lowk ? FGMM_FAMILY_LOWK : -1;
+  // the fused low-K kernel measured faster than the tensor-core family up to K d = 512
+  if (lowk && (int64_t)K * d <= 512) return FGMM_FAMILY_LOWK;
   return tc ? FGMM_FAMILY_TC : FGMM_FAMILY_SIMT;
 }
 
@@ -67,7 +71,8 @@ int fgmm_version(void) { return 10000; }
 
 int fgmm_set_family(int family) {
   int prev = g_family;
-  if (family == FGMM_FAMILY_AUTO || family == FGMM_FAMILY_SIMT || family == FGMM_FAMILY_TC)
+  if (family == FGMM_FAMILY_AUTO || family == FGMM_FAMILY_SIMT || family == FGMM_FAMILY_TC ||
+      family == FGMM_FAMILY_LOWK)
     g_family = family;
   return prev;
 }
@@ -96,6 +101,7 @@ size_t fgmm_em_stats_workspace_bytes(int64_t N, int32_t d, int32_t K) {
   int fam = resolve_family(N, d, K);
   if (fam == FGMM_FAMILY_TC) return tc_workspace_bytes(N, d, K);
   if (fam == FGMM_FAMILY_SIMT) return simt_workspace_bytes(N, d, K);
+  if (fam == FGMM_FAMILY_LOWK) return lowk_workspace_bytes(N, d, K);
   return 0;
 }
 
@@ -118,6 +124,11 @@ int em_stats_impl(const float *X, const void *points, int64_t N, int32_t d, cons
     if (workspace_bytes < simt_workspace_bytes(N, d, K))
       return fail(FGMM_ERR_WORKSPACE, "workspace too small");
     return simt_em_stats(X, N, d, mu, var, log_pi, K, stats, log_normalizer, workspace, st, update);
+  }
+  if (fam == FGMM_FAMILY_LOWK) {
+    if (workspace_bytes < lowk_workspace_bytes(N, d, K))
+      return fail(FGMM_ERR_WORKSPACE, "workspace too small");
+    return lowk_em_stats(X, N, d, mu, var, log_pi, K, stats, log_normalizer, workspace, st, update);
   }
   size_t need = tc_workspace_bytes(N, d, K);
   const void *pts = points;
@@ -245,6 +256,7 @@ int fgmm_device_error(int reset) { return tc_device_error(reset != 0); }
 int fgmm_em_stats_launches(int64_t N, int32_t d, int32_t K) {
   const int fam = resolve_family(N, d, K);
   if (fam == FGMM_FAMILY_SIMT) return simt_launches();
+  if (fam == FGMM_FAMILY_LOWK) return lowk_launches();
   if (fam == FGMM_FAMILY_TC) return tc_launches(N, d, K);
   return 0;
 }

@@ -111,6 +111,14 @@ int simt_em_stats(const float *X, int64_t N, int d, const float *mu, const float
                   const float *log_pi, int K, double *stats, float *log_norm,
                   void *ws, cudaStream_t stream, const UpdateOut *update = nullptr);
 
+// ---- low-K family (fgmm_lowk.cu): K <= 16, d <= 128, two launches per iteration ----
+bool lowk_supported(int64_t N, int d, int K);
+int lowk_launches();
+size_t lowk_workspace_bytes(int64_t N, int d, int K);
+int lowk_em_stats(const float *X, int64_t N, int d, const float *mu, const float *var,
+                  const float *log_pi, int K, double *stats, float *log_norm, void *ws,
+                  cudaStream_t stream, const UpdateOut *update = nullptr);
+
 // ---- tcgen05 family (fgmm_tc.cu) ----
 bool tc_supported(int64_t N, int d, int K);
 size_t tc_points_bytes(int64_t N, int d);

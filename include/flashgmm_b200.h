@@ -33,9 +33,11 @@ extern "C" {
 #define FGMM_ERR_CUDA 4         /* a CUDA runtime call or kernel launch failed */
 
 /* Kernel families fgmm_em_stats can run. */
-#define FGMM_FAMILY_AUTO 0      /* tcgen05 tensor-core kernels where the shape allows, else SIMT */
+#define FGMM_FAMILY_AUTO 0      /* low-K kernel for K <= 16, d <= 128, K d <= 512; else tcgen05
+                                   where the shape allows (d <= 128); else SIMT */
 #define FGMM_FAMILY_SIMT 1      /* force the generic fp32 CUDA-core kernels */
 #define FGMM_FAMILY_TC 2        /* require the tcgen05 kernels (error if the shape is outside them) */
+#define FGMM_FAMILY_LOWK 3      /* require the fused low-K kernel (K <= 16, d <= 128; error otherwise) */
 
 const char *fgmm_last_error(void);
 int fgmm_version(void);
@@ -44,7 +46,8 @@ int fgmm_version(void);
  * calls in this process (default FGMM_FAMILY_AUTO).  Returns the previous value. */
 int fgmm_set_family(int family);
 /* Which family fgmm_em_stats would run for this shape under the current setting
- * (FGMM_FAMILY_SIMT or FGMM_FAMILY_TC), or -1 if the shape is unsupported. */
+ * (FGMM_FAMILY_SIMT, FGMM_FAMILY_TC or FGMM_FAMILY_LOWK), or -1 if the shape is
+ * unsupported. */
 int fgmm_family_for(int64_t N, int32_t d, int32_t K);
 
 /* Length (in doubles) of the packed statistics vector: K*(2d+1)+1. */

@@ -28,25 +28,33 @@ from oracle import oracle
 pytestmark = pytest.mark.gpu
 
 TOL = {"mu": 1e-4, "var": 1e-4, "var_abs": 4e-6, "log_pi": 1e-4, "ln": 1e-3}
-SLACK_BY_FAMILY = {"simt": 1.5, "tc": 2.5, "auto": 2.5}
+SLACK_BY_FAMILY = {"simt": 1.5, "tc": 2.5, "lowk": 1.5, "auto": 2.5}
 SLACK = 2.5
 EM = [n for n in golden_names() if not n.startswith(("c1_fit20", "estep"))]
-FAMILIES = {"auto": 0, "simt": 1, "tc": 2}
+FAMILIES = {"auto": 0, "simt": 1, "tc": 2, "lowk": 3}
 
 
 @pytest.fixture(params=list(FAMILIES))
 def family(request):
-    """Run each test with the default selection, the generic SIMT kernels and the
-    tcgen05 kernels (the latter only for shapes they cover: d <= 128)."""
+    """Run each test with the default selection, the generic SIMT kernels, the tcgen05
+    kernels (shapes with d <= 128) and the fused low-K kernel (K <= 16, d <= 128)."""
     from flashgmm_b200 import flash_gmm_native as C
     prev = C.set_family(FAMILIES[request.param])
     yield request.param
     C.set_family(prev)
 
 
-def _skip_if_unsupported(family, d):
-    if family == "tc" and d > 128:
-        pytest.skip("tcgen05 family covers d <= 128")
+def _covered(family, K, d):
+    if family == "tc":
+        return d <= 128
+    if family == "lowk":
+        return K <= 16 and d <= 128
+    return True
+
+
+def _skip_if_unsupported(family, d, K=1):
+    if not _covered(family, K, d):
+        pytest.skip(f"the {family} family does not cover K={K} d={d}")
 
 
 def run_gpu(g):
@@ -72,7 +80,7 @@ def check(name, got, g, slack=SLACK):
 @pytest.mark.parametrize("name", EM)
 def test_flash_em_fused_parity(name, family):
     g = load_golden(name)
-    _skip_if_unsupported(family, g["X"].shape[1])
+    _skip_if_unsupported(family, g["X"].shape[1], g["mu"].shape[0])
     got = run_gpu(g)
     for a in got:
         assert np.all(np.isfinite(a))
@@ -123,6 +131,7 @@ def test_split_stats_update_equals_fused(family):
     """em_stats + em_update (the sharded-fit building blocks) == flash_em_fused."""
     from flashgmm_b200 import flash_gmm_native as C
     g = load_golden("c3_slice4096")
+    _skip_if_unsupported(family, g["X"].shape[1], g["mu"].shape[0])
     dev = torch.device("cuda:0")
     X, mu, var, lp = (torch.from_numpy(g[k]).to(dev) for k in ("X", "mu", "var", "log_pi"))
     fused = C.flash_em_fused(X, mu, var, lp)
@@ -138,6 +147,7 @@ def test_em_step_equals_split(family):
     """em_step (update fused into the reduction) == em_stats + em_update, also in place."""
     from flashgmm_b200 import flash_gmm_native as C
     g = load_golden("c2_slice2048")
+    _skip_if_unsupported(family, g["X"].shape[1], g["mu"].shape[0])
     dev = torch.device("cuda:0")
     X, mu, var, lp = (torch.from_numpy(g[k]).to(dev) for k in ("X", "mu", "var", "log_pi"))
     stats, ln = C.em_stats(X, mu, var, lp)
@@ -177,6 +187,7 @@ def test_sharded_stats_sum_equals_whole(family):
     """Stats of two halves summed == stats of the whole (the allreduce invariant)."""
     from flashgmm_b200 import flash_gmm_native as C
     g = load_golden("c2_slice2048")
+    _skip_if_unsupported(family, g["X"].shape[1], g["mu"].shape[0])
     dev = torch.device("cuda:0")
     X, mu, var, lp = (torch.from_numpy(g[k]).to(dev) for k in ("X", "mu", "var", "log_pi"))
     whole, _ = C.em_stats(X, mu, var, lp)
@@ -199,7 +210,7 @@ def test_tail_and_padding_sizes(family):
     dev = torch.device("cuda:0")
     for (N, K, d) in [(1, 1, 1), (129, 1, 32), (127, 129, 31), (300, 257, 64), (1000, 16, 96),
                       (515, 33, 160), (64, 3, 200), (4000, 200, 128), (257, 384, 33)]:
-        if family == "tc" and d > 128:
+        if not _covered(family, K, d):
             continue
         X, *_ = make_mixture(N, K, d, seed=N * 7 + K)
         if K <= N:
@@ -224,6 +235,7 @@ def test_point_chunks(family):
     from flashgmm_b200.data import make_mixture, init_params
     dev = torch.device("cuda:0")
     N, K, d = 120000, 1100, 16  # 256 MB blocks: 58,240 points per chunk, 3 chunks (ragged)
+    _skip_if_unsupported(family, d, K)
     if family == "tc":
         assert _lib.load().fgmm_em_stats_launches(N, d, K) >= 2 + 3 * 3, "expected >= 3 chunks"
     X, *_ = make_mixture(N, K, d, seed=11)
