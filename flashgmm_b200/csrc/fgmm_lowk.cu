@@ -10,7 +10,8 @@
 //   prologue  the direct-form parameters s = var^-1/2, m = mu s (fp64, rounded once) and
 //             lc = log_pi - 1/2 (d log 2pi + sum log var) of all K components into
 //             shared memory (what simt_prep_kernel computes, per block: no launch);
-//   stage     the tile's rows of X into shared memory (float4 when d % 4 == 0);
+//   stage     the tile's rows of X into shared memory with cp.async (16-byte pieces when
+//             d % 4 == 0), double-buffered: the next tile's copies run during this one;
 //   phase 1   four threads per point (interleaved quarters of the dimensions, summed by
 //             a shuffle tree, so no fp32 sum runs longer than d/4 terms) evaluate the K
 //             log-likelihoods in the reference's direct form
@@ -53,13 +54,25 @@ __host__ __device__ inline LkGeom lk_geom(int d) {
 }
 constexpr int kLkFold = 16;  // points a thread sums in fp32 before folding into fp64
 inline int lk_cpt(int d, int K) { return (K * lk_geom(d).D4 + kLkThreads - 1) / kLkThreads; }
-// [X tile | gamma tile | s | m | lc] floats, then per-thread fp64 accumulators
+// [X tile x 2 | gamma tile | s | m | lc] floats, then per-thread fp64 accumulators
 // [cpt * 9][256] (an even float count precedes them: 8-byte aligned).
 inline size_t lk_smem_floats(int d, int K) {
   const LkGeom g = lk_geom(d);
-  return (size_t)kLkTile * g.XS + (size_t)kLkTile * kLkGS + 2 * (size_t)K * g.dp4 + kLkMaxK +
+  return 2 * (size_t)kLkTile * g.XS + (size_t)kLkTile * kLkGS + 2 * (size_t)K * g.dp4 + kLkMaxK +
          2 * (size_t)lk_cpt(d, K) * 9 * kLkThreads;
 }
+
+// Asynchronous global -> shared copies (cp.async); src_bytes = 0 writes zeros.
+__device__ __forceinline__ void cpa16(float *dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src),
+               "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cpa4(float *dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src),
+               "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cpa_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cpa_wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 template <int CPT>  // components per phase-2 thread: ceil(K * D4 / 256), 1 or 2
 __global__ void __launch_bounds__(kLkThreads, 2)
@@ -69,8 +82,8 @@ lowk_stats_kernel(const float *__restrict__ X, int64_t N, int d, const float *__
                   double *__restrict__ ln_part, int vec) {
   extern __shared__ __align__(16) float lk_sm[];
   const LkGeom g = lk_geom(d);
-  float *x_s = lk_sm;                        // [kLkTile][XS]
-  float *gm_s = x_s + kLkTile * g.XS;        // [kLkTile][kLkGS]
+  float *x_s = lk_sm;                        // [2][kLkTile][XS] (double buffer)
+  float *gm_s = x_s + 2 * kLkTile * g.XS;    // [kLkTile][kLkGS]
   float *s_s = gm_s + kLkTile * kLkGS;       // [K][dp4]
   float *m_s = s_s + K * g.dp4;              // [K][dp4]
   float *lc_s = m_s + K * g.dp4;             // [kLkMaxK]
@@ -116,31 +129,48 @@ lowk_stats_kernel(const float *__restrict__ X, int64_t N, int d, const float *__
   double lnacc = 0.0;
 
   const int64_t ntiles = (N + kLkTile - 1) / kLkTile;
-  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    const int64_t n0 = tile * kLkTile;
-    const int np = N - n0 < kLkTile ? (int)(N - n0) : kLkTile;
-    __syncthreads();  // previous tile's phase 2 is done with x_s / gm_s (and the prologue)
-    if (vec) {
-      const float4 *src = reinterpret_cast<const float4 *>(X + n0 * d);
-      for (int i = t; i < kLkTile * g.D4; i += kLkThreads) {
-        const int p = i / g.D4, q = i - p * g.D4;
-        const float4 v = p < np ? __ldg(src + (int64_t)p * g.D4 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-        *reinterpret_cast<float4 *>(x_s + p * g.XS + 4 * q) = v;
-      }
-    } else {
-      for (int i = t; i < kLkTile * g.dp4; i += kLkThreads) {
-        const int p = i / g.dp4, j = i - p * g.dp4;
-        x_s[p * g.XS + j] = (p < np && j < d) ? __ldg(X + (n0 + p) * d + j) : 0.0f;
+  // stage a tile's rows into buffer b (zero-filled past N and past d); one commit group
+  auto stage = [&](int64_t tl, int b) {
+    if (tl < ntiles) {
+      const int64_t m0 = tl * kLkTile;
+      const int mp = N - m0 < kLkTile ? (int)(N - m0) : kLkTile;
+      float *dst = x_s + b * kLkTile * g.XS;
+      if (vec) {
+        const float4 *src = reinterpret_cast<const float4 *>(X + m0 * d);
+        for (int i = t; i < kLkTile * g.D4; i += kLkThreads) {
+          const int p = i / g.D4, q = i - p * g.D4;
+          const bool in = p < mp;
+          cpa16(dst + p * g.XS + 4 * q, in ? (const void *)(src + (int64_t)p * g.D4 + q) : (const void *)X,
+                in ? 16u : 0u);
+        }
+      } else {
+        for (int i = t; i < kLkTile * g.dp4; i += kLkThreads) {
+          const int p = i / g.dp4, j = i - p * g.dp4;
+          const bool in = p < mp && j < d;
+          cpa4(dst + p * g.XS + j, in ? (const void *)(X + (m0 + p) * d + j) : (const void *)X,
+               in ? 4u : 0u);
+        }
       }
     }
+    cpa_commit();
+  };
+  stage(blockIdx.x, 0);
+  int cur = 0;
+  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, cur ^= 1) {
+    const int64_t n0 = tile * kLkTile;
+    const int np = N - n0 < kLkTile ? (int)(N - n0) : kLkTile;
+    __syncthreads();  // the previous tile's phases are done with gm_s and the other buffer
+    stage(tile + gridDim.x, cur ^ 1);  // the next tile's rows fly during this tile
+    cpa_wait_prev();                   // this thread's copies of the current tile landed
     __syncthreads();
+    const float *xb = x_s + cur * kLkTile * g.XS;
 
     // phase 1
     {
       float acc[kLkMaxK];
 #pragma unroll
       for (int k = 0; k < kLkMaxK; ++k) acc[k] = 0.0f;
-      const float *xr = x_s + p1 * g.XS;
+      const float *xr = xb + p1 * g.XS;
       for (int i = sub; i < g.D4; i += kLkTPP) {
         const float4 xv = *reinterpret_cast<const float4 *>(xr + 4 * i);
 #pragma unroll
@@ -201,7 +231,7 @@ lowk_stats_kernel(const float *__restrict__ X, int64_t N, int d, const float *__
           for (int e = 0; e < 4; ++e) { as[c][e] = 0.0f; aq[c][e] = 0.0f; }
         }
         for (int p = pb; p < pe; p += PS) {
-          const float4 xv = *reinterpret_cast<const float4 *>(x_s + p * g.XS + 4 * j4);
+          const float4 xv = *reinterpret_cast<const float4 *>(xb + p * g.XS + 4 * j4);
 #pragma unroll
           for (int c = 0; c < CPT; ++c) {
             const int k = cg * CPT + c;
