@@ -74,8 +74,10 @@ __device__ __forceinline__ void cpa4(float *dst, const void *src, uint32_t src_b
 __device__ __forceinline__ void cpa_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cpa_wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
-template <int CPT>  // components per phase-2 thread: ceil(K * D4 / 256), 1 or 2
-__global__ void __launch_bounds__(kLkThreads, 2)
+// CPT: components per phase-2 thread, ceil(K * D4 / 256) (1 or 2); KM: the most
+// components the build handles (8: a 64-register build, four blocks per SM; 16: two).
+template <int CPT, int KM>
+__global__ void __launch_bounds__(kLkThreads, KM <= 8 ? 4 : 2)
 lowk_stats_kernel(const float *__restrict__ X, int64_t N, int d, const float *__restrict__ mu,
                   const float *__restrict__ var, const float *__restrict__ log_pi, int K,
                   float *__restrict__ ln_out, float *__restrict__ partial,
@@ -167,14 +169,14 @@ lowk_stats_kernel(const float *__restrict__ X, int64_t N, int d, const float *__
 
     // phase 1
     {
-      float acc[kLkMaxK];
+      float acc[KM];
 #pragma unroll
-      for (int k = 0; k < kLkMaxK; ++k) acc[k] = 0.0f;
+      for (int k = 0; k < KM; ++k) acc[k] = 0.0f;
       const float *xr = xb + p1 * g.XS;
       for (int i = sub; i < g.D4; i += kLkTPP) {
         const float4 xv = *reinterpret_cast<const float4 *>(xr + 4 * i);
 #pragma unroll
-        for (int k = 0; k < kLkMaxK; ++k) {
+        for (int k = 0; k < KM; ++k) {
           if (k < K) {
             const float4 sv = *reinterpret_cast<const float4 *>(s_s + k * g.dp4 + 4 * i);
             const float4 mv = *reinterpret_cast<const float4 *>(m_s + k * g.dp4 + 4 * i);
@@ -193,7 +195,7 @@ lowk_stats_kernel(const float *__restrict__ X, int64_t N, int d, const float *__
       // thread's exponentials for components k = sub (mod 4) only
       float mx = -FLT_MAX;
 #pragma unroll
-      for (int k = 0; k < kLkMaxK; ++k) {
+      for (int k = 0; k < KM; ++k) {
         if (k < K) {
           acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], 1);
           acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], 2);
@@ -203,14 +205,14 @@ lowk_stats_kernel(const float *__restrict__ X, int64_t N, int d, const float *__
       }
       float sum = 0.0f;
 #pragma unroll
-      for (int k = 0; k < kLkMaxK; ++k)
+      for (int k = 0; k < KM; ++k)
         if (k < K && (k & 3) == sub) sum += expf(acc[k] - mx);
       sum += __shfl_xor_sync(0xffffffffu, sum, 1);
       sum += __shfl_xor_sync(0xffffffffu, sum, 2);
       const float ln = mx + logf(sum);
       const bool live = p1 < np;
 #pragma unroll
-      for (int k = 0; k < kLkMaxK; ++k)
+      for (int k = 0; k < KM; ++k)
         if (k < K && (k & 3) == sub) gm_s[p1 * kLkGS + k] = live ? expf(acc[k] - ln) : 0.0f;
       if (live && sub == 0) {
         ln_out[n0 + p1] = ln;
@@ -285,10 +287,14 @@ lowk_stats_kernel(const float *__restrict__ X, int64_t N, int d, const float *__
   }
 }
 
-int lowk_blocks(int64_t N, int d, int K) {
+int lowk_blocks_per_sm(int d, int K) {
   const size_t smem = lk_smem_floats(d, K) * sizeof(float);
-  const int bps = (int)std::max<size_t>(1, std::min<size_t>(2, (size_t)(220 * 1024) / smem));
-  return (int)std::min<int64_t>(cdiv(N, kLkTile), (int64_t)bps * num_sms());
+  const int by_regs = K <= 8 ? 4 : 2;
+  return (int)std::max<size_t>(1, std::min<size_t>(by_regs, (size_t)(220 * 1024) / smem));
+}
+
+int lowk_blocks(int64_t N, int d, int K) {
+  return (int)std::min<int64_t>(cdiv(N, kLkTile), (int64_t)lowk_blocks_per_sm(d, K) * num_sms());
 }
 
 struct LkWs {
@@ -327,24 +333,22 @@ int lowk_em_stats(const float *X, int64_t N, int d, const float *mu, const float
   const size_t smem = lk_smem_floats(d, K) * sizeof(float);
   const int vec = (d % 4 == 0 && reinterpret_cast<uintptr_t>(X) % 16 == 0) ? 1 : 0;
   const int cpt = lk_cpt(d, K);
-  static bool attr_done[2] = {};
-  if (cpt == 1) {
-    if (!attr_done[0]) {
-      FGMM_CUDA_TRY(cudaFuncSetAttribute(lowk_stats_kernel<1>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
-      attr_done[0] = true;
+  auto go = [&](auto kernel, int slot) -> int {
+    static bool attr_done[3] = {};
+    if (!attr_done[slot]) {
+      FGMM_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+      FGMM_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+      attr_done[slot] = true;
     }
-    FGMM_CUDA_TRY(launch_pdl(lowk_stats_kernel<1>, w.slots, kLkThreads, smem, st, X, N, d, mu, var,
-                             log_pi, K, log_norm, w.partial, w.ln_part, vec));
-  } else {
-    if (!attr_done[1]) {
-      FGMM_CUDA_TRY(cudaFuncSetAttribute(lowk_stats_kernel<2>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
-      attr_done[1] = true;
-    }
-    FGMM_CUDA_TRY(launch_pdl(lowk_stats_kernel<2>, w.slots, kLkThreads, smem, st, X, N, d, mu, var,
-                             log_pi, K, log_norm, w.partial, w.ln_part, vec));
-  }
+    FGMM_CUDA_TRY(launch_pdl(kernel, w.slots, kLkThreads, smem, st, X, N, d, mu, var, log_pi, K,
+                             log_norm, w.partial, w.ln_part, vec));
+    return FGMM_OK;
+  };
+  int rc;
+  if (K <= 8) rc = go(lowk_stats_kernel<1, 8>, 0);
+  else if (cpt == 1) rc = go(lowk_stats_kernel<1, 16>, 1);
+  else rc = go(lowk_stats_kernel<2, 16>, 2);
+  if (rc) return rc;
   mark(st, "lowk_stats_kernel");
   return reduce_partials(w.partial, w.slots, K, d, g.dp4, g.W, w.ln_part, w.slots, stats, st, update);
 }
