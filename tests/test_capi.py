@@ -46,6 +46,26 @@ def test_size_queries_without_gpu():
     assert lib.fgmm_family_for(0, 8, 4) == -1
 
 
+def test_family_selection_without_gpu():
+    """FGMM_FAMILY_AUTO: low-K for K <= 16, d <= 128 and K d <= 512; tcgen05 for other
+    d <= 128; SIMT above.  A forced family the shape is outside of reports -1."""
+    lib = _lib.load()
+    assert lib.fgmm_family_for(4096, 32, 8) == _lib.FAMILY_LOWK
+    assert lib.fgmm_family_for(1000, 32, 16) == _lib.FAMILY_LOWK    # K d = 512
+    assert lib.fgmm_family_for(1000, 64, 16) == _lib.FAMILY_TC      # K d = 1024
+    assert lib.fgmm_family_for(1000, 2, 17) == _lib.FAMILY_TC       # K > 16
+    assert lib.fgmm_family_for(1000, 160, 2) == _lib.FAMILY_SIMT    # d > 128
+    prev = lib.fgmm_set_family(_lib.FAMILY_LOWK)
+    try:
+        assert lib.fgmm_family_for(1000, 128, 16) == _lib.FAMILY_LOWK
+        assert lib.fgmm_family_for(1000, 128, 17) == -1
+        assert lib.fgmm_family_for(1000, 129, 2) == -1
+        assert lib.fgmm_em_stats_launches(1000, 128, 16) == 2
+        assert lib.fgmm_em_stats_workspace_bytes(1000, 128, 16) > 0
+    finally:
+        lib.fgmm_set_family(prev)
+
+
 def test_invalid_arguments_report_errors():
     lib = _lib.load()
     rc = lib.fgmm_em_fused(None, 0, 8, None, None, None, 4, None, None, None, None, None, 0, None)

@@ -49,15 +49,6 @@ def test_lowk_matches_reference(lowk, N, K, d):
     check(f"lowk N={N} K={K} d={d}", got, g, SLACK_BY_FAMILY["lowk"])
 
 
-def test_auto_selects_lowk_for_small_k():
-    from flashgmm_b200 import flash_gmm_native as C
-    assert C.family_for(4096, 32, 8) == 3
-    assert C.family_for(1000, 32, 16) == 3   # K d = 512
-    assert C.family_for(1000, 64, 16) == 2   # K d = 1024: tensor cores
-    assert C.family_for(1000, 2, 17) == 2    # K > 16
-    assert C.family_for(1000, 160, 2) == 1   # d > 128: SIMT
-
-
 def test_lowk_step_split_and_shards(lowk):
     """em_step == em_stats + em_update, and the statistics of two halves add up to the
     whole's (the all-reduce invariant of a sharded fit)."""
