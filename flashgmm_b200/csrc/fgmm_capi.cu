@@ -37,6 +37,14 @@ int num_sms() {
   return cached[dev];
 }
 
+bool &device_once_flag(int slot) {
+  static bool flags[64][16] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  return flags[dev][slot & 15];
+}
+
 static int check_shape(int64_t N, int d, int K) {
   if (N < 1 || K < 1 || d < 1)
     return fail(FGMM_ERR_INVALID, "N, K and d must all be >= 1 (got N=" + std::to_string(N) +

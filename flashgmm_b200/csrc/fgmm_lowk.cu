@@ -19,12 +19,14 @@
 //             w w), then the log-sum-exp (max, then sum of expf) and
 //             gamma_k = expf(l_k - ln) into shared memory, ln to the output;
 //   phase 2   threads own (component group, 4 dimensions, point residue) cells and
-//             accumulate n_k, s_k = sum gamma x and sq_k = sum gamma x^2 in registers
-//             across all of the block's tiles (replaces the reference's per-block shared
-//             accumulators and global atomics, flash_gmm/csrc/flash_gmm_cuda.cu:179-292).
-// At the end the point-residue groups are added in a fixed order into one fp32 partial
-// row per (component, block), in reduce_rows4_kernel's layout [s (dp4) | sq (dp4) | n |
-// pad], and one fp64 log-normalizer sum per block.  Deterministic: no atomics.
+//             accumulate n_k, s_k = sum gamma x and sq_k = sum gamma x^2 in fp32 over
+//             at most 16 points, then fold them into their own fp64 slots in shared
+//             memory, across all of the block's tiles (replaces the reference's
+//             per-block shared accumulators and global atomics,
+//             flash_gmm/csrc/flash_gmm_cuda.cu:179-292).
+// At the end the point-residue groups' fp64 sums are added in a fixed order into one fp32
+// partial row per (component, block), in reduce_rows4_kernel's layout [s (dp4) | sq (dp4)
+// | n | pad], and one fp64 log-normalizer sum per block.  Deterministic: no atomics.
 #include <float.h>
 #include <algorithm>
 #include "fgmm_common.cuh"
@@ -334,11 +336,11 @@ int lowk_em_stats(const float *X, int64_t N, int d, const float *mu, const float
   const int vec = (d % 4 == 0 && reinterpret_cast<uintptr_t>(X) % 16 == 0) ? 1 : 0;
   const int cpt = lk_cpt(d, K);
   auto go = [&](auto kernel, int slot) -> int {
-    static bool attr_done[3] = {};
-    if (!attr_done[slot]) {
+    bool &done = device_once_flag(slot);
+    if (!done) {
       FGMM_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
       FGMM_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-      attr_done[slot] = true;
+      done = true;
     }
     FGMM_CUDA_TRY(launch_pdl(kernel, w.slots, kLkThreads, smem, st, X, N, d, mu, var, log_pi, K,
                              log_norm, w.partial, w.ln_part, vec));

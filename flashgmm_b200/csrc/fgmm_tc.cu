@@ -1111,13 +1111,13 @@ int tc_launch_chunk(const TcPlan &p, const TcChunk &c, int64_t n0, bool first, c
 template <int NKC>
 int tc_launch(const TcPlan &p, const float *X, const float *pts, const TcWs &w, float *ln,
               cudaStream_t st) {
-  static bool attr_done[5] = {};
-  if (!attr_done[NKC / 2]) {
+  bool &done = device_once_flag(8 + NKC / 2);
+  if (!done) {
     FGMM_CUDA_TRY(cudaFuncSetAttribute(tc_pass1_kernel<NKC>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1_bytes()));
     FGMM_CUDA_TRY(cudaFuncSetAttribute(tc_stats_kernel<NKC>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2_bytes(NKC * KC)));
-    attr_done[NKC / 2] = true;
+    done = true;
   }
   for (int i = 0; i < p.chunks; ++i) {
     const int64_t n0 = (int64_t)i * p.Nc;
