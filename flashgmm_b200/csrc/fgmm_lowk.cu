@@ -77,9 +77,10 @@ __device__ __forceinline__ void cpa_commit() { asm volatile("cp.async.commit_gro
 __device__ __forceinline__ void cpa_wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 // CPT: components per phase-2 thread, ceil(K * D4 / 256) (1 or 2); KM: the most
-// components the build handles (8: a 64-register build, four blocks per SM; 16: two).
+// components the build handles (8: a 64-register build, four blocks per SM; 16: three
+// blocks per SM with one component per phase-2 thread, two with two).
 template <int CPT, int KM>
-__global__ void __launch_bounds__(kLkThreads, KM <= 8 ? 4 : 2)
+__global__ void __launch_bounds__(kLkThreads, KM <= 8 ? 4 : (CPT == 1 ? 3 : 2))
 lowk_stats_kernel(const float *__restrict__ X, int64_t N, int d, const float *__restrict__ mu,
                   const float *__restrict__ var, const float *__restrict__ log_pi, int K,
                   float *__restrict__ ln_out, float *__restrict__ partial,
@@ -291,7 +292,7 @@ lowk_stats_kernel(const float *__restrict__ X, int64_t N, int d, const float *__
 
 int lowk_blocks_per_sm(int d, int K) {
   const size_t smem = lk_smem_floats(d, K) * sizeof(float);
-  const int by_regs = K <= 8 ? 4 : 2;
+  const int by_regs = K <= 8 ? 4 : (lk_cpt(d, K) == 1 ? 3 : 2);  // the builds' launch bounds
   return (int)std::max<size_t>(1, std::min<size_t>(by_regs, (size_t)(220 * 1024) / smem));
 }
 
