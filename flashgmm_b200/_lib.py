@@ -17,6 +17,7 @@ FGMM_ERR_UNSUPPORTED = 2
 FGMM_ERR_WORKSPACE = 3
 FGMM_ERR_CUDA = 4
 FAMILY_AUTO, FAMILY_SIMT, FAMILY_TC, FAMILY_LOWK = 0, 1, 2, 3
+UPDATE_NO_FLOORS = 1
 
 # (name, restype, argtypes) for every symbol the header declares.
 _vp, _i64, _i32, _sz, _d = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_size_t, ctypes.c_double
@@ -31,6 +32,7 @@ SIGNATURES = {
     "fgmm_em_stats_workspace_bytes": (_sz, [_i64, _i32, _i32]),
     "fgmm_em_stats": (ctypes.c_int, [_vp, _vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _sz, _vp]),
     "fgmm_em_update": (ctypes.c_int, [_vp, _d, _i32, _i32, _vp, _vp, _vp, _vp]),
+    "fgmm_em_update_ex": (ctypes.c_int, [_vp, _d, _i32, _i32, _i32, _vp, _vp, _vp, _vp]),
     "fgmm_em_step": (ctypes.c_int, [_vp, _vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp,
                                     _vp, _sz, _i32, _vp]),
     "fgmm_device_error": (ctypes.c_int, [ctypes.c_int]),
@@ -83,3 +85,20 @@ def check(rc):
         msg = load().fgmm_last_error()
         raise FlashGMMError(rc, msg.decode() if msg else "")
     return rc
+
+
+class DeviceWaitError(RuntimeError):
+    """A tensor-core kernel gave up a bounded wait: the results of that launch (and of
+    every launch since) are incomplete."""
+
+
+def check_device_error():
+    """Raise :class:`DeviceWaitError` if a tensor-core kernel recorded a wait timeout on
+    the current device since the last check (the code is cleared).  Synchronises the
+    device: call it where the host already waits for results."""
+    code = load().fgmm_device_error(1)
+    if code < 0:
+        raise DeviceWaitError("fgmm_device_error: CUDA error while reading the device error word")
+    if code:
+        raise DeviceWaitError(f"a tensor-core kernel gave up a bounded wait (code {code}); "
+                              "the results of this iteration are incomplete")

@@ -1,5 +1,6 @@
 // extern "C" entry points declared in include/flashgmm_b200.h.
 #include <cstdio>
+#include <atomic>
 #include <mutex>
 #include "fgmm_common.cuh"
 
@@ -23,22 +24,24 @@ PhaseTimer *&phase_timer() {
   return t;
 }
 
+// Caches shared by every host thread: atomics, so concurrent first calls on one device
+// race benignly (both compute the same value) and never tear.
 int num_sms() {
-  static int cached[64] = {0};
+  static std::atomic<int> cached[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
-  if (!cached[dev]) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
-      n = 148;
-    cached[dev] = n;
+  int v = cached[dev].load(std::memory_order_acquire);
+  if (!v) {
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+      v = 148;
+    cached[dev].store(v, std::memory_order_release);
   }
-  return cached[dev];
+  return v;
 }
 
-bool &device_once_flag(int slot) {
-  static bool flags[64][16] = {};
+std::atomic<bool> &device_once_flag(int slot) {
+  static std::atomic<bool> flags[64][16];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
@@ -188,6 +191,16 @@ int fgmm_em_update(const double *stats, double n_total, int32_t K, int32_t d, fl
   if (!stats || !new_mu || !new_var || !new_log_pi) return fail(FGMM_ERR_INVALID, "null pointer");
   if (!(n_total > 0)) return fail(FGMM_ERR_INVALID, "n_total must be > 0");
   return em_update(stats, n_total, K, d, new_mu, new_var, new_log_pi, (cudaStream_t)stream);
+}
+
+int fgmm_em_update_ex(const double *stats, double n_total, int32_t K, int32_t d, int32_t flags,
+                      float *new_mu, float *new_var, float *new_log_pi, void *stream) {
+  if (K < 1 || d < 1) return fail(FGMM_ERR_INVALID, "K and d must be >= 1");
+  if (!stats || !new_mu || !new_var || !new_log_pi) return fail(FGMM_ERR_INVALID, "null pointer");
+  if (!(n_total > 0)) return fail(FGMM_ERR_INVALID, "n_total must be > 0");
+  if (flags & ~FGMM_UPDATE_NO_FLOORS) return fail(FGMM_ERR_INVALID, "unknown flags");
+  return em_update(stats, n_total, K, d, new_mu, new_var, new_log_pi, (cudaStream_t)stream,
+                   (flags & FGMM_UPDATE_NO_FLOORS) == 0);
 }
 
 size_t fgmm_em_fused_workspace_bytes(int64_t N, int32_t d, int32_t K) {

@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stddef.h>
+#include <atomic>
 #include <string>
 
 #include "../../include/flashgmm_b200.h"
@@ -75,7 +76,7 @@ struct Carve {
 int num_sms();
 // Per-device "done" flag for one-time kernel attribute settings (cudaFuncSetAttribute
 // applies to the current device only): flag `slot` (< 16) of the current device.
-bool &device_once_flag(int slot);
+std::atomic<bool> &device_once_flag(int slot);
 
 // Optional per-launch event recording (active only inside fgmm_em_stats_profiled).
 struct PhaseTimer {

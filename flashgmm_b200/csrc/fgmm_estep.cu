@@ -27,9 +27,9 @@ estep_ll_kernel(const float *__restrict__ X, int64_t N, int d, const float *__re
   __shared__ float xs[kEPts][kEDim + 1];
   __shared__ float ss[kEDim][kEComps], mm[kEDim][kEComps];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int tk = blockIdx.x;
+  const int tk = blockIdx.y;  // component tiles in y (K / 32 <= 65535), point tiles in x
   const int k = tk * kEComps + lane;
-  const int64_t n0 = (int64_t)blockIdx.y * kEPts;
+  const int64_t n0 = (int64_t)blockIdx.x * kEPts;
   float acc[8];
 #pragma unroll
   for (int p = 0; p < 8; ++p) acc[p] = 0.0f;
@@ -127,7 +127,9 @@ int estep(const float *X, int64_t N, int d, const float *mu, const float *var, c
   const EstepWs w = estep_layout(ws, N, d, K);
   int rc = prep_direct_params(mu, var, log_pi, K, d, w.sc, w.ms, w.lc, st);
   if (rc) return rc;
-  dim3 grid(w.T, (unsigned)cdiv(N, kEPts));
+  if (cdiv(N, kEPts) > 0x7fffffff || w.T > 65535)
+    return fail(FGMM_ERR_UNSUPPORTED, "E-step: N or K beyond the launch grid");
+  dim3 grid((unsigned)cdiv(N, kEPts), w.T);
   estep_ll_kernel<<<grid, 256, 0, st>>>(X, N, d, w.sc, w.ms, w.lc, K, gamma, w.part_m, w.part_s, w.T);
   FGMM_LAUNCH_CHECK("estep_ll_kernel");
   estep_norm_kernel<<<(unsigned)cdiv(N, 8), 256, 0, st>>>(N, K, w.T, w.part_m, w.part_s, gamma, log_norm);

@@ -337,7 +337,7 @@ int lowk_em_stats(const float *X, int64_t N, int d, const float *mu, const float
   const int vec = (d % 4 == 0 && reinterpret_cast<uintptr_t>(X) % 16 == 0) ? 1 : 0;
   const int cpt = lk_cpt(d, K);
   auto go = [&](auto kernel, int slot) -> int {
-    bool &done = device_once_flag(slot);
+    std::atomic<bool> &done = device_once_flag(slot);
     if (!done) {
       FGMM_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
       FGMM_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));

@@ -1111,7 +1111,7 @@ int tc_launch_chunk(const TcPlan &p, const TcChunk &c, int64_t n0, bool first, c
 template <int NKC>
 int tc_launch(const TcPlan &p, const float *X, const float *pts, const TcWs &w, float *ln,
               cudaStream_t st) {
-  bool &done = device_once_flag(8 + NKC / 2);
+  std::atomic<bool> &done = device_once_flag(8 + NKC / 2);
   if (!done) {
     FGMM_CUDA_TRY(cudaFuncSetAttribute(tc_pass1_kernel<NKC>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1_bytes()));

@@ -93,6 +93,9 @@ class DistributedFlashGMM:
             stats = self._allreduce(stats.clone(), it)
             mu, var, log_pi = self.update_fn(stats, n_total, self.K, self.d)
             avg_ll = stats[-1].item() / n_total
+            if X_local.is_cuda and self.stats_fn is _gpu_stats:
+                from . import _lib
+                _lib.check_device_error()
             self.log_normalizer = ln
             history.append({"iter": it, "log_likelihood": avg_ll,
                             "time_ms": (time.time() - t0) * 1000})

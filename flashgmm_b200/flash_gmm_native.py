@@ -21,7 +21,8 @@ import torch
 
 from . import _lib
 
-__all__ = ["flash_em_fused", "standard_e_step", "flash_e_step", "standard_m_step", "em_stats",
+__all__ = ["flash_em_fused", "standard_e_step", "flash_e_step", "standard_m_step", "em_stats", "em_step",
+           "StatsWorkspace",
            "em_update", "prepare_points", "stats_len", "family_for", "set_family"]
 
 
@@ -242,8 +243,12 @@ def em_step(X, mu, var, log_pi, points=None, workspace=None, out=None, prepared=
     return out[0], out[1], out[2], workspace.stats, workspace.ln
 
 
-def em_update(stats, n_total, K, d, out=None):
-    """M-step from (summed) stats -> ``(new_mu, new_var, new_log_pi)``."""
+def em_update(stats, n_total, K, d, out=None, floors=True):
+    """M-step from (summed) stats -> ``(new_mu, new_var, new_log_pi)``.
+
+    ``floors=True`` is the fused op's update (n_k and the weight floored at 1e-8,
+    ``flash_gmm/csrc/flash_gmm_cpu.cpp:270-284``); ``floors=False`` the pure-Python
+    model's (``flash_gmm/flash_gmm.py:162-169``): no floor, only the variance clamped."""
     if stats.dtype != torch.float64 or not stats.is_cuda or stats.numel() != stats_len(K, d):
         raise RuntimeError("stats must be a CUDA float64 tensor of length K(2d+1)+1")
     dev = stats.device
@@ -253,6 +258,7 @@ def em_update(stats, n_total, K, d, out=None):
             out = (torch.empty(K, d, dtype=torch.float32, device=dev),
                    torch.empty(K, d, dtype=torch.float32, device=dev),
                    torch.empty(K, dtype=torch.float32, device=dev))
-        _lib.check(lib.fgmm_em_update(stats.data_ptr(), float(n_total), K, d, out[0].data_ptr(),
-                                      out[1].data_ptr(), out[2].data_ptr(), _stream_ptr(dev)))
+        _lib.check(lib.fgmm_em_update_ex(stats.data_ptr(), float(n_total), K, d,
+                                         0 if floors else _lib.UPDATE_NO_FLOORS, out[0].data_ptr(),
+                                         out[1].data_ptr(), out[2].data_ptr(), _stream_ptr(dev)))
     return out

@@ -17,6 +17,7 @@ import time
 
 import torch
 
+from . import _lib
 from . import flash_gmm_native as _C
 
 
@@ -85,6 +86,7 @@ class NativeStandardGMM(_EMModel):
             t0 = time.time()
             gamma, log_norm = _C.standard_e_step(X, self.mu, self.var, self.log_pi)
             avg_ll = log_norm.mean().item()
+            _lib.check_device_error()
             self.mu, self.var, self.log_pi = _C.standard_m_step(X, gamma)
             elapsed = time.time() - t0
             history.append({"iter": it, "log_likelihood": avg_ll, "time_ms": elapsed * 1000})
@@ -99,7 +101,8 @@ class NativeStandardGMM(_EMModel):
 
 
 class NativeFlashGMM(_EMModel):
-    """Flash-GMM EM on B200 kernels (no N x K matrix is ever materialised)."""
+    """Flash-GMM EM on B200 kernels: each iteration is the fused statistics launch
+    sequence plus the M-step; the N x K responsibilities are never returned or kept."""
 
     def __init__(self, K: int, d: int, BN: int = 64, BK: int = 8,
                  max_iter: int = 100, tol: float = 1e-4, seed: int = 42, device=None):
@@ -148,6 +151,7 @@ class NativeFlashGMM(_EMModel):
                 X, self.mu, self.var, self.log_pi, points=points, workspace=ws,
                 prepared=self._reuse and it > 0)
             avg_ll = stats[-1].item() / N
+            _lib.check_device_error()
             self.log_normalizer = log_norm
             elapsed = time.time() - t0
             history.append({"iter": it, "log_likelihood": avg_ll, "time_ms": elapsed * 1000})
@@ -195,6 +199,7 @@ class NativeFlashGMM(_EMModel):
             t0 = time.time()
             graph.replay()
             lls = (h_ll / N).tolist()  # one synchronisation per replay
+            _lib.check_device_error()
             elapsed = (time.time() - t0) * 1000 / G
             for i in range(G):
                 if it >= self.max_iter:

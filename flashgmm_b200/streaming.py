@@ -13,6 +13,7 @@ import time
 
 import torch
 
+from . import _lib
 from . import flash_gmm_native as _C
 
 
@@ -104,6 +105,7 @@ class StreamingFlashGMM:
                     freed[b].record(comp)
                 self.mu, self.var, self.log_pi = _C.em_update(acc, N, self.K, d)
                 avg_ll = acc[-1].item() / N
+                _lib.check_device_error()
                 elapsed = time.time() - t0
                 history.append({"iter": it, "log_likelihood": avg_ll, "time_ms": elapsed * 1000})
                 if verbose and (it % 10 == 0 or it < 5):

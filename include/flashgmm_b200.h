@@ -86,6 +86,14 @@ int fgmm_em_stats(const float *X, const void *points, int64_t N, int32_t d,
 int fgmm_em_update(const double *stats, double n_total, int32_t K, int32_t d,
                    float *new_mu, float *new_var, float *new_log_pi, void *stream);
 
+/* fgmm_em_update with options.  flags = 0 is fgmm_em_update.  FGMM_UPDATE_NO_FLOORS
+ * applies the pure-Python model's update instead (reference flash_gmm/flash_gmm.py:162-169,
+ * FlashGMM._fused_em_step): mu = s/n, var = max(sq/n - mu^2, 1e-6), log_pi = log(n/n_total),
+ * with no floor on n or on the weight (an empty component gives NaN / -inf, as there). */
+#define FGMM_UPDATE_NO_FLOORS 1
+int fgmm_em_update_ex(const double *stats, double n_total, int32_t K, int32_t d, int32_t flags,
+                      float *new_mu, float *new_var, float *new_log_pi, void *stream);
+
 /* One EM iteration on one device over prepared points: fgmm_em_stats followed by
  * the M-step of fgmm_em_update (n_total = N), the update applied inside the
  * statistics reduction's launch.  `stats` and `log_normalizer` are written as by

@@ -23,8 +23,20 @@ OUT = os.path.join(HERE, "_ref")
 NAME = "flash_gmm_ref"
 
 
+def default_reference_root():
+    """The reference checkout: ``$FLASHGMM_REFERENCE``, else a ``reference`` directory
+    beside this repository, else None."""
+    env = os.environ.get("FLASHGMM_REFERENCE")
+    if env:
+        return env
+    sib = os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+    return sib if os.path.isdir(os.path.join(sib, "flash_gmm", "csrc")) else None
+
+
 def build(ref_root=None, verbose=False):
-    ref_root = ref_root or os.environ.get("FLASHGMM_REFERENCE", "/root/reference")
+    ref_root = ref_root or default_reference_root()
+    if not ref_root:
+        raise FileNotFoundError("no reference checkout: set FLASHGMM_REFERENCE")
     csrc = os.path.join(ref_root, "flash_gmm", "csrc")
     srcs = [os.path.join(csrc, "binding.cpp"), os.path.join(csrc, "flash_gmm_cpu.cpp")]
     for s in srcs:

@@ -30,6 +30,12 @@ def golden_names(prefix=""):
     return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, prefix + "*.npz")))
 
 
+def em_golden_names():
+    """The one-iteration flash_em_fused fixtures (config slices and ragged edge cases)."""
+    return [n for n in golden_names() if n.startswith(("c1_iter", "c2_slice", "c3_slice", "c4_slice",
+                                                         "c5_slice", "edge_"))]
+
+
 def load_golden(name):
     with np.load(os.path.join(GOLDEN, name + ".npz")) as z:
         return {k: z[k] for k in z.files}

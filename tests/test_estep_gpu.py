@@ -142,3 +142,21 @@ def test_predict():
     assert p.shape == (X.shape[0], g["mu"].shape[0])
     assert torch.allclose(p.sum(1), torch.ones(X.shape[0], device=DEV), atol=1e-5)
     assert torch.equal(m.predict(X), p.argmax(1))
+
+
+def test_e_step_beyond_the_old_grid_limit():
+    """N = 4,194,368 points (more than 65,535 tiles of 64): the point tiles run in the
+    launch grid's x dimension, which covers any N.  Compared with the reference
+    algorithm's fp32 evaluation (the C restatement) against fp64."""
+    from flashgmm_b200 import flash_gmm_native as C
+    from flashgmm_b200.data import make_mixture, init_params
+    N, K, d = 4 * 1024 * 1024 + 64, 4, 8
+    X, *_ = make_mixture(N, K, d, seed=21)
+    mu, var, lp = init_params(X[:4096], K, seed=22)
+    gam, ln = [o.cpu().numpy() for o in C.standard_e_step(_t(X.numpy()), _t(mu.numpy()),
+                                                         _t(var.numpy()), _t(lp.numpy()))]
+    rg, rln = oracle.standard_e_step(X, mu, var, lp)
+    for idx in (slice(0, 4096), slice(N - 4096, N)):  # both ends of the grid
+        check_estep(gam[idx], ln[idx], rg[idx], rln[idx], X.numpy()[idx], mu.numpy(), var.numpy(),
+                    lp.numpy())
+    assert np.all(np.isfinite(ln))

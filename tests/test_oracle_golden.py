@@ -7,10 +7,10 @@ restatement must reproduce them bit for bit.
 import numpy as np
 import pytest
 
-from helpers import golden_names, load_golden, param_errors
+from helpers import em_golden_names, load_golden, param_errors
 from oracle import oracle
 
-EM = [n for n in golden_names() if not n.startswith(("c1_fit20", "estep"))]
+EM = em_golden_names()
 
 
 @pytest.mark.parametrize("name", EM)
@@ -56,3 +56,19 @@ def test_fp64_restatement_close_to_reference(name):
     e = param_errors([g["new_mu"], g["new_var"], g["new_log_pi"], g["log_normalizer"]], r64[:4],
                      n_k=r64[4], N=N)
     assert e["ln"] < 5e-3 and e["log_pi"] < 1e-3 and e["mu"] < 1e-2, e
+
+
+@pytest.mark.parametrize("name", ["c3_fit20_n16384"])
+def test_fit20_fixture_pinned(name):
+    """The 20-iteration fixtures store no X: the regenerated workload must match the
+    stored digest, and the first step of the bit-exact restatement (and of the fp64
+    restatement) must reproduce the stored first log-likelihoods."""
+    import hashlib
+    from flashgmm_b200.data import make_workload
+    g = load_golden(name)
+    X, *_ = make_workload(str(g["workload"]), N=int(g["N"]))
+    assert hashlib.sha256(X.numpy().tobytes()).hexdigest() == str(g["x_sha256"])
+    out = oracle.flash_em_fused(X, g["mu0"], g["var0"], g["log_pi0"], BK=8, nthreads=int(g["nthreads"]))
+    assert abs(float(np.mean(out[3].astype(np.float64))) - float(g["ll"][0])) < 1e-9
+    r = oracle.flash_em_fused_f64(X, g["mu0"], g["var0"], g["log_pi0"])
+    assert abs(float(np.mean(r[3])) - float(g["ll64"][0])) < 1e-9

@@ -22,7 +22,7 @@ import numpy as np
 import pytest
 import torch
 
-from helpers import golden_names, load_golden, param_errors
+from helpers import em_golden_names, load_golden, param_errors
 from oracle import oracle
 
 pytestmark = pytest.mark.gpu
@@ -30,7 +30,7 @@ pytestmark = pytest.mark.gpu
 TOL = {"mu": 1e-4, "var": 1e-4, "var_abs": 4e-6, "log_pi": 1e-4, "ln": 1e-3}
 SLACK_BY_FAMILY = {"simt": 1.5, "tc": 2.5, "lowk": 1.5, "auto": 2.5}
 SLACK = 2.5
-EM = [n for n in golden_names() if not n.startswith(("c1_fit20", "estep"))]
+EM = em_golden_names()
 FAMILIES = {"auto": 0, "simt": 1, "tc": 2, "lowk": 3}
 
 
