@@ -7,6 +7,7 @@
 #include <string>
 
 #include "../../include/flashgmm_b200.h"
+#include "fgmm_tcops.cuh"
 
 namespace fgmm {
 
@@ -102,11 +103,10 @@ struct UpdateOut {
   double n_total;
   float *mu, *var, *log_pi;
   bool floors;
-  // Optional (tensor-core family, d <= 128): also write the next iteration's pass-1
-  // operands for the updated parameters, as tc_prep_params_kernel would (dp = 0: off).
-  float *qhi = nullptr, *qlo = nullptr, *cst2 = nullptr, *sc = nullptr, *ms = nullptr,
-        *lc = nullptr;
-  int dp = 0;
+  // Optional (tensor-core family, d <= 128): also write the next iteration's
+  // parameter operands for the updated parameters, as tc_prep_params_kernel would
+  // (tc.kbp = 0: off).
+  TcParamOps tc;
 };
 
 // ---- SIMT family (fgmm_simt.cu) ----

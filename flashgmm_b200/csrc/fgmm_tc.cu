@@ -1,36 +1,24 @@
 // tcgen05 tensor-core family of the fused EM statistics kernels (sm_100a).
 //
-// Both passes evaluate the Mahalanobis term through the expansion
-//   sum_j (x_j - mu_kj)^2 / var_kj = sum_j x_j^2 iv_kj - 2 sum_j x_j mu_kj iv_kj + sum_j mu_kj^2 iv_kj
-// as one GEMM per (point tile, component tile):
-//   acc[n,k] = P[n,:] . Q[k,:],   P[n] = [x^2 | x],  Q[k] = [iv | -2 mu iv]
-// with the constant folded into cst2_k = log2(e) (log_pi - 1/2 (d log 2pi + sum log var + sum mu^2 iv)),
-// so that log2-likelihood = cst2_k - (log2(e)/2) acc.  The GEMM runs in 3xTF32: every
-// operand is split v = hi + lo with hi, lo tf32, and acc += lo_P.hi_Q + hi_P.lo_Q + hi_P.hi_Q.
-// (Reference: the direct form in flash_gmm/csrc/flash_gmm_cuda.cu:135-156 and
-// flash_gmm/csrc/flash_gmm_cpu.cpp:30-45.)
-//
-// Pass 1 (log-normalizer): persistent CTAs over (point tile, component group) units;
-//   the accumulator lives in TMEM and eight epilogue warps run the online log-sum-exp of
-//   flash_gmm/csrc/flash_gmm_cuda.cu:145-155 in base 2, writing one (max, sum) partial
-//   per point and component group.
-// Pass 2 (statistics): CTA (component tile ct, slot) walks a contiguous range of point
-//   tiles.  Per tile: the distance GEMM again -> gamma = 2^(l2 - ln2) computed by the
-//   epilogue from TMEM and stored to shared memory -> a second GEMM
-//   S[k, f] = sum_n gamma[n,k] F[n,f],  F[n] = [x^2 | x] (hi + lo), and
-//   n_k = sum_n gamma[n,k] on the CUDA cores.  gamma is split into tf32 hi + lo (three
-//   products) and staged in two 64-point rounds; S restarts every tile and is added
-//   (fp32, round-to-nearest) into one partial row per CTA; the partials are reduced in
-//   fp64 afterwards: deterministic, no atomics between CTAs.  (Reference: flash_accumulate_stats_v2_kernel,
-//   flash_gmm/csrc/flash_gmm_cuda.cu:179-292, which accumulates with global atomics.)
-//
-// Warp roles (320 threads): warp 0 issues TMA loads, warp 1 owns TMEM and issues
-// tcgen05.mma (one thread), warps 2-9 are the epilogue: warp w reads TMEM lanes
-// 32*(w%4) .. +31, and warps w and w+4 split the 128 columns of a tile.  No cluster
-// multicast anywhere.
+// Per iteration, over chunks of points:
+//   tc_pass1_kernel   distance GEMM D = P Q^T (kind::f16, fp16 hi/lo operands, the
+//                     per-dimension [x^2, x, 1] . [iv, -2 mu iv, mu^2 iv] layout of
+//                     fgmm_tcops.cuh), the online log-sum-exp of
+//                     flash_gmm/csrc/flash_gmm_cuda.cu:145-155 in base 2, the four
+//                     leading components of every point, and the log2-likelihood block
+//                     Lt [component][point] that the statistics pass reads;
+//   tc_refine_kernel  merges the component groups, re-evaluates the leading components
+//                     exactly in the reference's direct form, writes the log-normalizer;
+//   tc_stats_kernel   S[k, f] = sum_n gamma[n, k] F[n, f], F = [x^2 | x] (kind::f16,
+//                     gamma from tensor memory), one partial row per (component, CTA).
+// (Reference: flash_log_normalizer_v2_kernel and flash_accumulate_stats_v2_kernel,
+// flash_gmm/csrc/flash_gmm_cuda.cu:72-292, and the direct form of
+// flash_gmm/csrc/flash_gmm_cpu.cpp:30-45.)  No cluster multicast anywhere.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <cuda_fp16.h>
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <mutex>
 
@@ -42,27 +30,42 @@ using namespace ptx;
 
 namespace {
 
-constexpr int BM = 128;                       // points per tile
-constexpr int NC = 128;                       // components per tile
-constexpr int KC = 32;                        // fp32 elements per K chunk (one 128-byte row)
-constexpr int kEpiWarps = 16;                 // four warps per TMEM lane quarter
-constexpr int kThreads = 64 + 32 * kEpiWarps; // warp 0 TMA, warp 1 MMA, warps 2.. epilogue
+constexpr int BM = 128;                        // points per pass-1 tile (MMA M)
+constexpr int KCH = 64;                        // fp16 K elements per staged chunk (128-byte rows)
+constexpr int kEpiWarps = 16;                  // four warps per TMEM lane quarter
+constexpr int kThreads1 = 64 + 32 * kEpiWarps; // warp 0 TMA, warp 1 MMA, warps 2.. epilogue
 constexpr int kEpiThreads = 32 * kEpiWarps;
-constexpr int kPart = 32;                     // columns of a tile owned by one epilogue warp
-constexpr int kParts = NC / kPart;            // epilogue warps per lane quarter
-constexpr int kStages1 = 3;
-constexpr int kTileBytes = BM * KC * 4;       // 16 KB: 128 rows x 128 B
-constexpr int kStageBytes = 4 * kTileBytes;   // 64 KB
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
-constexpr int kMaxDp = 128;                   // d <= 128 runs here
+constexpr int kMaxD = 128;                     // d <= 128 runs here
+// Leading components more than kNear below a point's largest base-2 log-likelihood have
+// responsibilities below 2^-kNear relative to the leader and are not re-evaluated.
+#ifndef FGMM_NEAR
+#define FGMM_NEAR 32.0f
+#endif
+constexpr float kNear = FGMM_NEAR;
 
-// Points buffer: P_hi and P_lo, each [Npad][2 dp] fp32 with Npad = N rounded up to a
-// whole 128-row tile (rows >= N are zero), so no TMA box ever leaves the tensor.
-inline int dp_of(int d) { return (d + KC - 1) / KC * KC; }
 inline int64_t npad_of(int64_t N) { return cdiv(N, BM) * BM; }
-inline size_t points_half_floats(int64_t N, int d) {
-  return align_up((size_t)npad_of(N) * 2 * dp_of(d), 256);
+
+// Prepared points: header (column exponents, max |x|), then P hi / lo [Npad][KBp] and
+// F hi / lo [Npad][KA], fp16.  Rows >= N are zero, so no TMA box leaves the tensor.
+inline size_t p_elems(int64_t N, int d) { return align_up((size_t)npad_of(N) * tc_kbp(d), 128); }
+inline size_t f_elems(int64_t N, int d) { return align_up((size_t)npad_of(N) * 2 * tc_dp(d), 128); }
+struct PtsPtrs {
+  const int *aexp;
+  uint32_t *xmax;
+  __half *phi, *plo, *fhi, *flo;
+};
+inline PtsPtrs pts_ptrs(const void *pts, int64_t N, int d) {
+  char *b = static_cast<char *>(const_cast<void *>(pts));
+  PtsPtrs p;
+  p.aexp = reinterpret_cast<const int *>(b + kPtsAexpOff);
+  p.xmax = reinterpret_cast<uint32_t *>(b + kPtsXmaxOff);
+  p.phi = reinterpret_cast<__half *>(b + kPtsHeader);
+  p.plo = p.phi + p_elems(N, d);
+  p.fhi = p.plo + p_elems(N, d);
+  p.flo = p.fhi + f_elems(N, d);
+  return p;
 }
 
 __device__ __forceinline__ uint8_t *align1024(uint8_t *p) {
@@ -70,76 +73,69 @@ __device__ __forceinline__ uint8_t *align1024(uint8_t *p) {
   return reinterpret_cast<uint8_t *>((a + 1023) & ~uintptr_t(1023));
 }
 
+__device__ __forceinline__ void split_f16f(float v, __half &hi, __half &lo) {
+  hi = __float2half_rn(v);
+  lo = __float2half_rn(v - __half2float(hi));
+}
+
 // --------------------------------------------------------------------------- prep
-// P[n] = [x^2 (dp) | x (dp)] split into tf32 hi/lo (zero for j >= d and rows n >= N).
+// max |x_j| over the points (one thread per dimension, a row range per block).
+__global__ void __launch_bounds__(128) tc_xmax_kernel(const float *__restrict__ X, int64_t N, int d,
+                                                      uint32_t *__restrict__ xmax) {
+  const int j = threadIdx.x;
+  if (j >= d) return;
+  float m = 0.0f;
+  for (int64_t n = blockIdx.x; n < N; n += gridDim.x) m = fmaxf(m, fabsf(__ldg(X + n * d + j)));
+  atomicMax(xmax + j, __float_as_uint(m));  // non-negative floats order like their bits
+}
+
+// P[n][c] (c = 3 j + t: x^2, x, 1) and F[n][f] (f < dp: x^2, else x), scaled by the
+// column exponents and split into fp16 hi / lo; the threads of row 0 also record the
+// exponents of P.
 __global__ void tc_prep_points_kernel(const float *__restrict__ X, int64_t N, int64_t Npad, int d,
-                                      int dp, float *__restrict__ phi, float *__restrict__ plo) {
-  const int KA = 2 * dp;
-  const int64_t total = Npad * dp;
+                                      int kbp, int ka, const uint32_t *__restrict__ xmax,
+                                      int *__restrict__ aexp, __half *__restrict__ phi,
+                                      __half *__restrict__ plo, __half *__restrict__ fhi,
+                                      __half *__restrict__ flo) {
+  const int W = kbp + ka, dp = ka / 2;
+  const int64_t total = Npad * W;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t n = i / dp;
-    const int j = (int)(i - n * dp);
-    const float x = (j < d && n < N) ? __ldg(X + n * d + j) : 0.0f;
-    const float x2 = x * x;
-    const float x2h = to_tf32(x2), xh = to_tf32(x);
-    phi[n * KA + j] = x2h;
-    plo[n * KA + j] = to_tf32(x2 - x2h);
-    phi[n * KA + dp + j] = xh;
-    plo[n * KA + dp + j] = to_tf32(x - xh);
+    const int64_t n = i / W;
+    const int c = (int)(i - n * W);
+    int j, t;
+    if (c < kbp) { j = c / 3; t = c - 3 * j; }
+    else { const int f = c - kbp; t = f < dp ? 0 : 1; j = t == 0 ? f : f - dp; }
+    const bool in = j < d;
+    const int a = in ? tc_p_col_exp(3 * j + t, d, xmax) : 0;
+    const float x = (in && n < N) ? __ldg(X + n * d + j) : 0.0f;
+    const float v = ldexpf(t == 0 ? x * x : (t == 1 ? x : (in && n < N ? 1.0f : 0.0f)), a);
+    __half hi, lo;
+    split_f16f(v, hi, lo);
+    if (c < kbp) {
+      phi[n * kbp + c] = hi;
+      plo[n * kbp + c] = lo;
+      if (n == 0) aexp[c] = a;
+    } else {
+      fhi[n * ka + (c - kbp)] = hi;
+      flo[n * ka + (c - kbp)] = lo;
+    }
   }
 }
 
-// Q[k] = [iv (dp) | -2 mu iv (dp)] (hi/lo of the fp64 value), cst2[k]; rows k >= K are
-// zero with cst2 = -inf (padding components never receive responsibility).
-// Also writes the direct-form parameters the refinement uses: sc = var^{-1/2},
-// ms = mu sc, lc = log_pi - 1/2 (d log 2pi + sum log var)  ([K][d], [K][d], [K]).
-__global__ void tc_prep_params_kernel(const float *__restrict__ mu, const float *__restrict__ var,
-                                      const float *__restrict__ log_pi, int K, int d, int dp,
-                                      float *__restrict__ qhi, float *__restrict__ qlo,
-                                      float *__restrict__ cst2, float *__restrict__ sc,
-                                      float *__restrict__ ms, float *__restrict__ lc) {
+// One block of 128 threads per component (rows k >= K are padding: zero operands,
+// cst2 = -inf, so they never receive responsibility).
+__global__ void __launch_bounds__(128)
+tc_prep_params_kernel(const float *__restrict__ mu, const float *__restrict__ var,
+                      const float *__restrict__ log_pi, int K, int d, TcParamOps op) {
   griddep_launch();
   griddep_wait();
-  const int k = blockIdx.x;
-  const int KA = 2 * dp;
-  __shared__ double red[8], red2[8];
-  double acc = 0.0;   // sum_j (log var + mu^2 / var)
-  double acc2 = 0.0;  // sum_j log var
-  for (int j = threadIdx.x; j < dp; j += blockDim.x) {
-    double iv = 0.0, b = 0.0;
-    if (k < K && j < d) {
-      const double v = var[(int64_t)k * d + j];
-      const double m = mu[(int64_t)k * d + j];
-      iv = 1.0 / v;
-      b = -2.0 * m * iv;
-      acc += log(v) + m * m * iv;
-      acc2 += log(v);
-      const double sv = 1.0 / sqrt(v);
-      sc[(int64_t)k * d + j] = (float)sv;
-      ms[(int64_t)k * d + j] = (float)(m * sv);
-    }
-    const float ivh = to_tf32((float)iv), bh = to_tf32((float)b);
-    qhi[(int64_t)k * KA + j] = ivh;
-    qlo[(int64_t)k * KA + j] = to_tf32((float)(iv - (double)ivh));
-    qhi[(int64_t)k * KA + dp + j] = bh;
-    qlo[(int64_t)k * KA + dp + j] = to_tf32((float)(b - (double)bh));
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    acc2 += __shfl_xor_sync(0xffffffffu, acc2, o);
-  }
-  if ((threadIdx.x & 31) == 0) { red[threadIdx.x >> 5] = acc; red2[threadIdx.x >> 5] = acc2; }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    double t = 0.0, t2 = 0.0;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { t += red[w]; t2 += red2[w]; }
-    cst2[k] = (k < K) ? (float)(1.4426950408889634 *
-                                ((double)log_pi[k] - 0.5 * (d * kLog2Pi + t)))
-                      : -INFINITY;
-    if (k < K) lc[k] = (float)((double)log_pi[k] - 0.5 * (d * kLog2Pi + t2));
-  }
+  const int k = blockIdx.x, j = threadIdx.x;
+  const bool live = k < K && j < d;
+  const float m32 = live ? mu[(int64_t)k * d + j] : 0.0f;
+  const float v32 = live ? var[(int64_t)k * d + j] : 1.0f;
+  const float lp = k < K ? log_pi[k] : 0.0f;
+  tc_prep_component(k, K, d, j, m32, v32, lp, op, 1);
 }
 
 // ------------------------------------------------------------- shared pieces
@@ -156,103 +152,103 @@ __device__ __forceinline__ bool epi_sync_and(bool v) {
   return r != 0;
 }
 
-// The distance GEMM is accumulated per 32-column K group (one staged chunk): each group
-// goes into a fresh TMEM buffer, the 8 small cross products (lo.hi, hi.lo) first and the
-// 4 hi.hi products last, and the epilogue adds the groups in fp32 registers.
-// Tensor-memory accumulation does not round to nearest, so one long accumulation at the
-// magnitude of the expanded form (|x|^2/var ~ thousands) drifts by ~1e-2; short groups
-// with the small terms summed first, added on the CUDA cores, match a direct fp32
-// evaluation of the Mahalanobis sum.
-
-// K group size in staged 32-column chunks (divides NKC).
-#ifndef FGMM_GROUP_CHUNKS
-#define FGMM_GROUP_CHUNKS 1
-#endif
-template <int NKC>
-__host__ __device__ constexpr int group_chunks() {
-  constexpr int g = FGMM_GROUP_CHUNKS < NKC ? FGMM_GROUP_CHUNKS : NKC;
-  return NKC % g == 0 ? g : (NKC % 2 == 0 ? 2 : 1);
+// Pushes (x, ix) into (tv, ti), the four largest values seen in descending order (ties:
+// first seen), and returns in (dv, di) the one of the five that drops out (di = -1 for
+// an empty slot, whose value is -inf).
+__device__ __forceinline__ void top_push(float (&tv)[kTcTop], int (&ti)[kTcTop], float x, int ix,
+                                         float &dv, int &di) {
+  if (!(x > tv[3])) { dv = x; di = ix; return; }
+  dv = tv[3]; di = ti[3];
+  if (x > tv[1]) {
+    tv[3] = tv[2]; ti[3] = ti[2];
+    tv[2] = tv[1]; ti[2] = ti[1];
+    if (x > tv[0]) { tv[1] = tv[0]; ti[1] = ti[0]; tv[0] = x; ti[0] = ix; }
+    else           { tv[1] = x; ti[1] = ix; }
+  } else if (x > tv[2]) {
+    tv[3] = tv[2]; ti[3] = ti[2]; tv[2] = x; ti[2] = ix;
+  } else {
+    tv[3] = x; ti[3] = ix;
+  }
 }
 
-// MMA side: one staged 32-column chunk of a K group that rotates over NB TMEM buffers;
-// gfirst / glast mark the group's first / last chunk.
-// `desc` is the stage's shared-memory descriptor (SWIZZLE_128B K-major, stage base); the
-// operand tiles and k-steps are fixed offsets of its 16-byte address field, so the issuing
-// thread (which shares its scheduler with a quarter of the epilogue warps) spends one add
-// per operand.
-template <int NB>
-__device__ __forceinline__ bool issue_dist_chunk(uint64_t desc, uint32_t tmem, uint32_t &gcount,
-                                                 uint32_t tfull0, uint32_t tempty0, bool gfirst,
-                                                 bool glast) {
-  constexpr uint32_t idesc = idesc_tf32(BM, NC, 0, 0);
-  constexpr uint64_t kT = kTileBytes >> 4, kK = 32 >> 4;  // tile and k-step offsets
-  const uint32_t buf = gcount % NB, use = gcount / NB;
-  if (gfirst && !mbar_wait(tempty0 + 8u * buf, (use & 1u) ^ 1u, kErrWaitTmemEmpty)) return false;
-  tc_fence_after();
-  const uint32_t d = tmem + buf * NC;
-#pragma unroll
-  for (int kk = 0; kk < KC / 8; ++kk) {
-    mma_tf32(d, desc + kT + kk * kK, desc + 2 * kT + kk * kK, idesc, (kk != 0 || !gfirst) ? 1u : 0u);
-    mma_tf32(d, desc + kk * kK, desc + 3 * kT + kk * kK, idesc, 1u);
-  }
-#pragma unroll
-  for (int kk = 0; kk < KC / 8; ++kk) mma_tf32(d, desc + kk * kK, desc + 2 * kT + kk * kK, idesc, 1u);
-  if (glast) {
-    mma_commit(tfull0 + 8u * buf);
-    ++gcount;
-  }
-  return true;
+// Adds 2^v to the base-2 log-sum-exp state (m, s) = 2^m s.
+__device__ __forceinline__ void lse_add(float &m, float &s, float v) {
+  const float mn = fmaxf(m, v);
+  const float r = mn == -INFINITY ? 0.0f : mn;
+  s = s * ex2(m - r) + ex2(v - r);
+  m = mn;
 }
 
-// Epilogue side: add the next group buffer into acc (this warp's 32 rows, its 32 columns;
-// lane_tmem already points at the warp's lane quarter and column part).
-template <int NB, bool kFirst>
-__device__ __forceinline__ bool drain_group(uint32_t lane_tmem, uint32_t &gcount, uint32_t tfull0,
-                                            uint32_t tempty0, float (&acc)[kPart], int lane) {
-  const uint32_t buf = gcount % NB, use = gcount / NB;
-  if (!__all_sync(0xffffffffu, mbar_wait(tfull0 + 8u * buf, use & 1u, kErrWaitTmemFull)))
-    return false;
-  tc_fence_after();
-  float v[kPart];
-  tmem_ld32(lane_tmem + buf * NC, v);
-  tmem_wait_ld();
-#pragma unroll
-  for (int e = 0; e < kPart; ++e) acc[e] = kFirst ? v[e] : acc[e] + v[e];
-  tc_fence_before();
-  __syncwarp();
-  if (lane == 0) mbar_arrive(tempty0 + 8u * buf);
-  ++gcount;
-  return true;
+// Merges (m2, s2) into (m, s).
+__device__ __forceinline__ void lse_merge(float &m, float &s, float m2, float s2) {
+  const float mn = fmaxf(m, m2);
+  const float r = mn == -INFINITY ? 0.0f : mn;
+  s = s * ex2(m - r) + s2 * ex2(m2 - r);
+  m = mn;
+}
+
+// A point's running summary over the components seen so far: the four largest
+// log2-likelihoods with their components, and the base-2 log-sum-exp (m, s) of all the
+// others.  Keeping the two apart (every value that leaves the four joins the rest) lets
+// the refinement replace the four by exactly evaluated values without subtracting them
+// from a total, which loses everything when an approximate leader was far too large.
+__device__ __forceinline__ void summary_push(float (&tv)[kTcTop], int (&ti)[kTcTop], float &m, float &s,
+                                             float x, int ix) {
+  float dv;
+  int di;
+  top_push(tv, ti, x, ix, dv, di);
+  if (di >= 0) lse_add(m, s, dv);
 }
 
 // ------------------------------------------------------------------------- pass 1
-template <int NKC>
-__global__ void __launch_bounds__(kThreads, 1)
+// Persistent CTAs over (point tile, component group) units; a group is `tpg` component
+// tiles of NC.  Per tile the MMA thread accumulates all NKC chunks into one TMEM buffer
+// (two buffers, so the next tile's MMAs run while the epilogue drains this one):
+// per chunk four k-steps of lo.hi and hi.lo, then four of hi.hi (small products first).
+// Epilogue warp w owns TMEM lane quarter w % 4 (32 points) and a quarter of the tile's
+// columns; it turns accumulators into log2-likelihoods l2 = cst2 + coef D, stores them
+// into Lt (transposed, evict_last: the statistics pass reads them back), and keeps per
+// point an online (max, sum) and the four largest l2 with their components.
+template <int NKC, int NC>
+struct Pass1Shape {
+  static constexpr int S = NC == 256 ? 2 : 3;             // stages
+  static constexpr int kPBytes = BM * 128;                 // P tile of one chunk (hi or lo)
+  static constexpr int kQBytes = NC * 128;                 // Q tile of one chunk (hi or lo)
+  static constexpr int kStage = 2 * kPBytes + 2 * kQBytes;
+  static constexpr int kCols = NC / 4;                     // columns per epilogue warp
+  struct Part { float m, s; float v[kTcTop]; int i[kTcTop]; };
+  static constexpr int kBarOff = S * kStage;
+  static constexpr int kXOff = kBarOff + 8 * (2 * S + 5) + 8;
+  static constexpr int kSmem = 1024 + kXOff + 3 * BM * (int)sizeof(Part);
+};
+
+template <int NKC, int NC>
+__global__ void __launch_bounds__(kThreads1, 1)
 tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ CUtensorMap tm_plo,
                 const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant__ CUtensorMap tm_qlo,
-                const float *__restrict__ cst2, int64_t N, int n_pt, int n_ct, int G, int tpg,
-                float *__restrict__ part_m, float *__restrict__ part_s,
-                float2 *__restrict__ part_tv, int2 *__restrict__ part_ti,
-                float *__restrict__ Lt, int64_t Npad) {
-  constexpr int S = kStages1;
-  constexpr int NB = 4;  // TMEM group buffers (4 x 128 columns)
+                const float *__restrict__ coef, const float *__restrict__ cst2, int64_t N, int n_pt,
+                int n_ct, int G, int tpg, float *__restrict__ part_m, float *__restrict__ part_s,
+                float4 *__restrict__ part_tv, int4 *__restrict__ part_ti, float *__restrict__ Lt,
+                int64_t Npad) {
+  using Sh = Pass1Shape<NKC, NC>;
+  constexpr int S = Sh::S;
+  using Part = typename Sh::Part;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = align1024(smem_raw);
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * kStageBytes);
-  // bars: full[S] empty[S] tfull[NB] tempty[NB] done
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 2 * NB + 1);
-  struct Part { float m, s, v1, v2; int i1, i2; };
-  Part *lse_x = reinterpret_cast<Part *>(tmem_slot + 2);  // [kParts - 1][128] row exchange
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Sh::kBarOff);
+  // bars: full[S] empty[S] tfull[2] tempty[2] done
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 5);
+  Part *lse_x = reinterpret_cast<Part *>(smem + Sh::kXOff);  // [3][128] row exchange
   const uint32_t bar0 = smem_u32(bars);
   auto FULL = [&](int s) { return bar0 + 8u * s; };
   auto EMPTY = [&](int s) { return bar0 + 8u * (S + s); };
-  const uint32_t TFULL0 = bar0 + 8u * (2 * S), TEMPTY0 = bar0 + 8u * (2 * S + NB);
-  const uint32_t DONE = bar0 + 8u * (2 * S + 2 * NB);
+  const uint32_t TFULL0 = bar0 + 8u * (2 * S), TEMPTY0 = bar0 + 8u * (2 * S + 2);
+  const uint32_t DONE = bar0 + 8u * (2 * S + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) { mbar_init(FULL(s), 1); mbar_init(EMPTY(s), 1); }
-    for (int b = 0; b < NB; ++b) {
+    for (int b = 0; b < 2; ++b) {
       mbar_init(TFULL0 + 8u * b, 1);
       mbar_init(TEMPTY0 + 8u * b, kEpiWarps);
     }
@@ -260,7 +256,7 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_alloc(smem_u32(tmem_slot), 2 * NC);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -285,12 +281,13 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
         for (int t = g * tpg; t < t1 && ok; ++t) {
           for (int c = 0; c < NKC; ++c) {
             if (!mbar_wait(EMPTY(stage), phase ^ 1, kErrWaitEmpty)) { ok = false; break; }
-            const uint32_t base = smem_u32(smem + stage * kStageBytes);
-            mbar_arrive_expect_tx(FULL(stage), kStageBytes);
-            tma_load_2d_hint(base, &tm_phi, c * KC, pt * BM, FULL(stage), pol_p);
-            tma_load_2d_hint(base + kTileBytes, &tm_plo, c * KC, pt * BM, FULL(stage), pol_p);
-            tma_load_2d_hint(base + 2 * kTileBytes, &tm_qhi, c * KC, t * NC, FULL(stage), pol_q);
-            tma_load_2d_hint(base + 3 * kTileBytes, &tm_qlo, c * KC, t * NC, FULL(stage), pol_q);
+            const uint32_t base = smem_u32(smem + stage * Sh::kStage);
+            mbar_arrive_expect_tx(FULL(stage), Sh::kStage);
+            tma_load_2d_hint(base, &tm_phi, c * KCH, pt * BM, FULL(stage), pol_p);
+            tma_load_2d_hint(base + Sh::kPBytes, &tm_plo, c * KCH, pt * BM, FULL(stage), pol_p);
+            tma_load_2d_hint(base + 2 * Sh::kPBytes, &tm_qhi, c * KCH, t * NC, FULL(stage), pol_q);
+            tma_load_2d_hint(base + 2 * Sh::kPBytes + Sh::kQBytes, &tm_qlo, c * KCH, t * NC,
+                             FULL(stage), pol_q);
             armed |= 1u << stage;
             armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
             if (++stage == S) { stage = 0; phase ^= 1; }
@@ -299,146 +296,148 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
       }
       // never leave the CTA with bulk copies in flight
       for (int s = 0; s < S; ++s)
-        if (armed & (1u << s)) mbar_wait(FULL(s), (armed_par >> s) & 1u, kErrWaitDrain);
+        if (armed & (1u << s)) mbar_wait_drain(FULL(s), (armed_par >> s) & 1u);
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0, gcount = 0;
-      bool ok = true;
+      constexpr uint32_t idesc = idesc_f16(BM, NC, 0, 0);
+      constexpr uint64_t kPl = Sh::kPBytes >> 4, kQh = (2 * Sh::kPBytes) >> 4,
+                         kQl = (2 * Sh::kPBytes + Sh::kQBytes) >> 4;
       const uint64_t desc0 = sdesc_sw128(smem_u32(smem), 16, 1024);
+      int stage = 0;
+      uint32_t phase = 0, tcount = 0;
+      bool ok = true;
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
         const int g = u % G;
         const int t1 = min(n_ct, (g + 1) * tpg);
         for (int t = g * tpg; t < t1 && ok; ++t) {
+          const uint32_t buf = tcount & 1u, use = tcount >> 1;
+          if (!mbar_wait(TEMPTY0 + 8u * buf, (use & 1u) ^ 1u, kErrWaitTmemEmpty)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d = tmem + buf * NC;
           for (int c = 0; c < NKC; ++c) {
             if (!mbar_wait(FULL(stage), phase, kErrWaitFull)) { ok = false; break; }
             tc_fence_after();
-            constexpr int GC = group_chunks<NKC>();
-            if (!issue_dist_chunk<NB>(desc0 + (uint64_t)((stage * kStageBytes) >> 4), tmem, gcount,
-                                      TFULL0, TEMPTY0, c % GC == 0, c % GC == GC - 1)) {
-              ok = false;
-              break;
+            const uint64_t ds = desc0 + (uint64_t)((stage * Sh::kStage) >> 4);
+#pragma unroll
+            for (int kk = 0; kk < KCH / 16; ++kk) {  // k-step kk: +32 bytes = +2
+              mma_f16(d, ds + kPl + 2 * kk, ds + kQh + 2 * kk, idesc, (c != 0 || kk != 0) ? 1u : 0u);
+              mma_f16(d, ds + 2 * kk, ds + kQl + 2 * kk, idesc, 1u);
             }
+#pragma unroll
+            for (int kk = 0; kk < KCH / 16; ++kk) mma_f16(d, ds + 2 * kk, ds + kQh + 2 * kk, idesc, 1u);
             mma_commit(EMPTY(stage));
             if (++stage == S) { stage = 0; phase ^= 1; }
           }
+          if (!ok) break;
+          mma_commit(TFULL0 + 8u * buf);
+          ++tcount;
         }
       }
       mma_commit(DONE);
-      mbar_wait(DONE, 0, kErrWaitDrain);
+      mbar_wait_drain(DONE, 0);
     }
     __syncwarp();
   } else {
+    constexpr int kC = Sh::kCols;
     const int q = warp & 3, part = (warp - 2) >> 2;
     const int row = q * 32 + lane;
     const uint64_t pol_l = policy_evict_last();
-    const uint32_t lane_tmem = tmem + ((uint32_t)(q * 32) << 16) + part * kPart;
-    uint32_t gcount = 0;
+    const uint32_t lane_tmem = tmem + ((uint32_t)(q * 32) << 16) + part * kC;
+    uint32_t tcount = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
       const int pt = u / G, g = u % G;
       const int t1 = min(n_ct, (g + 1) * tpg);
-      float m = -INFINITY, s = 0.0f;
-      float v1 = -INFINITY, v2 = -INFINITY;  // the row's two largest log2-likelihoods
-      int i1 = -1, i2 = -1;
       const int64_t n_row = (int64_t)pt * BM + row;
+      float m = -INFINITY, s = 0.0f;
+      float tv[kTcTop] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      int ti[kTcTop] = {-1, -1, -1, -1};
       for (int t = g * tpg; t < t1 && ok; ++t) {
-        const int kb = t * NC + part * kPart;
-        float acc[kPart];
-        ok = drain_group<NB, true>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
-#pragma unroll 1
-        for (int grp = 1; grp < NKC / group_chunks<NKC>() && ok; ++grp)
-          ok = drain_group<NB, false>(lane_tmem, gcount, TFULL0, TEMPTY0, acc, lane);
+        const uint32_t buf = tcount & 1u, use = tcount >> 1;
+        ok = __all_sync(0xffffffffu, mbar_wait(TFULL0 + 8u * buf, use & 1u, kErrWaitTmemFull));
         if (!ok) break;
-        float cst[kPart];  // this warp's 32 log-coefficients (uniform loads, L1-resident)
-#pragma unroll
-        for (int e = 0; e < kPart; e += 4)
-          *reinterpret_cast<float4 *>(cst + e) = __ldg(reinterpret_cast<const float4 *>(cst2 + kb + e));
-        float c4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
-#pragma unroll
-        for (int e = 0; e < kPart; ++e) {
-          acc[e] = fmaf(acc[e], -0.5f * kLog2e, cst[e]);
-          c4[e & 3] = fmaxf(c4[e & 3], acc[e]);
-        }
-        const float cm = fmaxf(fmaxf(c4[0], c4[1]), fmaxf(c4[2], c4[3]));
-        {  // the log2-likelihood matrix feeds the statistics pass; stored transposed
-           // (Lt [component][point]) so that each store of a warp is 32 consecutive points
-          // kept in L2 for the statistics pass (evict_last)
-          float *lp = Lt + (int64_t)kb * Npad + n_row;
-#pragma unroll
-          for (int e = 0; e < kPart; ++e) st_hint(lp + (int64_t)e * Npad, acc[e], pol_l);
-        }
-        const float mn = fmaxf(m, cm);
-        const float mr = (mn == -INFINITY) ? 0.0f : mn;
-        float a4[4] = {s * ex2(m - mr), 0.0f, 0.0f, 0.0f};
-#pragma unroll
-        for (int e = 0; e < kPart; ++e) a4[e & 3] += ex2(acc[e] - mr);
-        s = (a4[0] + a4[1]) + (a4[2] + a4[3]);
-        m = mn;
-        if (cm > v2) {  // the tile's two largest, without data-dependent branches
-          int e1 = kPart;  // first column at the maximum
-#pragma unroll
-          for (int e = kPart - 1; e >= 0; --e) e1 = acc[e] == cm ? e : e1;
-          float t4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-          int k4[4] = {-1, -1, -1, -1};
-#pragma unroll
-          for (int e = 0; e < kPart; ++e) {
-            const bool take = e != e1 && acc[e] > t4[e & 3];
-            t4[e & 3] = take ? acc[e] : t4[e & 3];
-            k4[e & 3] = take ? e : k4[e & 3];
+        tc_fence_after();
+        const int kb = t * NC + part * kC;
+#pragma unroll 1
+        for (int h = 0; h < kC / 32; ++h) {  // 32 columns at a time (register budget)
+          float w[32];
+          tmem_ld32(lane_tmem + buf * NC + h * 32, w);
+          tmem_wait_ld();
+          if (h == kC / 32 - 1) {  // the buffer is drained: the MMA may refill it
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(TEMPTY0 + 8u * buf);
+            ++tcount;
           }
-          float t2 = t4[0];
-          int e2 = k4[0];
+          const int k0 = kb + h * 32;
+          float c4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
 #pragma unroll
-          for (int c = 1; c < 4; ++c)
-            if (t4[c] > t2 || (t4[c] == t2 && k4[c] >= 0 && (e2 < 0 || k4[c] < e2))) { t2 = t4[c]; e2 = k4[c]; }
-          auto insert = [&](float x, int ix) {
-            if (x > v2) {
-              if (x > v1) { v2 = v1; i2 = i1; v1 = x; i1 = ix; }
-              else        { v2 = x; i2 = ix; }
+          for (int e = 0; e < 32; e += 4) {
+            const float4 a = __ldg(reinterpret_cast<const float4 *>(coef + k0 + e));
+            const float4 b = __ldg(reinterpret_cast<const float4 *>(cst2 + k0 + e));
+            w[e] = fmaf(w[e], a.x, b.x);
+            w[e + 1] = fmaf(w[e + 1], a.y, b.y);
+            w[e + 2] = fmaf(w[e + 2], a.z, b.z);
+            w[e + 3] = fmaf(w[e + 3], a.w, b.w);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) c4[r] = fmaxf(c4[r], w[e + r]);
+          }
+          const float cm = fmaxf(fmaxf(c4[0], c4[1]), fmaxf(c4[2], c4[3]));
+#ifndef FGMM_EXP_NO_LT
+          {  // the log2-likelihood block, transposed: a warp's store is 32 consecutive points
+            float *lp = Lt + (int64_t)k0 * Npad + n_row;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) st_hint(lp + (int64_t)e * Npad, w[e], pol_l);
+          }
+#endif
+          // A value enters the leading four only if it lies within kNear of the point's
+          // running maximum (the refinement re-evaluates nothing further below); every
+          // other value, and every value the four push out, joins the rest, whose
+          // reference is its true maximum (so its sum never underflows to zero).
+          const float thr = fmaxf(tv[0], cm) - kNear;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            if (w[e] > thr && w[e] > tv[3]) {
+              int di;
+              top_push(tv, ti, w[e], k0 + e, w[e], di);  // w[e] becomes the dropped value
             }
-          };
-          if (e1 < kPart) {
-            insert(cm, kb + e1);
-            if (e2 >= 0) insert(t2, kb + e2);
           }
+          float r4[4] = {m, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r4[e & 3] = fmaxf(r4[e & 3], w[e]);
+          const float mn = fmaxf(fmaxf(r4[0], r4[1]), fmaxf(r4[2], r4[3]));
+          const float mr = (mn == -INFINITY) ? 0.0f : mn;
+          float a4[4] = {s * ex2(m - mr), 0.0f, 0.0f, 0.0f};
+#pragma unroll
+          for (int e = 0; e < 32; ++e) a4[e & 3] += ex2(w[e] - mr);  // a dropped empty slot: -inf
+          s = (a4[0] + a4[1]) + (a4[2] + a4[3]);
+          m = mn;
         }
       }
-      // merge the column parts of each row
-      if (part > 0) lse_x[(part - 1) * BM + row] = Part{m, s, v1, v2, i1, i2};
+      // merge the four column parts of each row
+      if (part > 0) {
+        Part &o = lse_x[(part - 1) * BM + row];
+        o.m = m; o.s = s;
+#pragma unroll
+        for (int r = 0; r < kTcTop; ++r) { o.v[r] = tv[r]; o.i[r] = ti[r]; }
+      }
       ok = epi_sync_and(ok);
       if (part == 0) {
-        Part o[kParts];
-        o[0] = Part{m, s, v1, v2, i1, i2};
 #pragma unroll
-        for (int r = 1; r < kParts; ++r) o[r] = lse_x[(r - 1) * BM + row];
-        float mn = -INFINITY;
+        for (int r = 0; r < 3; ++r) {
+          const Part &o = lse_x[r * BM + row];
+          lse_merge(m, s, o.m, o.s);
 #pragma unroll
-        for (int r = 0; r < kParts; ++r) mn = fmaxf(mn, o[r].m);
-        const float mr = (mn == -INFINITY) ? 0.0f : mn;
-        float sm = 0.0f;
-        float b1 = -INFINITY, b2 = -INFINITY;
-        int j1 = -1, j2 = -1;
-#pragma unroll
-        for (int r = 0; r < kParts; ++r) {
-          sm += o[r].s * ex2(o[r].m - mr);
-          const float c[2] = {o[r].v1, o[r].v2};
-          const int ci[2] = {o[r].i1, o[r].i2};
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            if (c[e] > b2) {
-              if (c[e] > b1) { b2 = b1; j2 = j1; b1 = c[e]; j1 = ci[e]; }
-              else           { b2 = c[e]; j2 = ci[e]; }
-            }
-          }
+          for (int c = 0; c < kTcTop; ++c)
+            if (o.i[c] >= 0) summary_push(tv, ti, m, s, o.v[c], o.i[c]);
         }
         const int64_t n = (int64_t)pt * BM + row;
         if (ok && n < N) {
-          part_m[(int64_t)g * N + n] = mn;
-          part_s[(int64_t)g * N + n] = sm;
-          part_tv[(int64_t)g * N + n] = make_float2(b1, b2);
-          part_ti[(int64_t)g * N + n] = make_int2(j1, j2);
+          part_m[(int64_t)g * N + n] = m;
+          part_s[(int64_t)g * N + n] = s;
+          part_tv[(int64_t)g * N + n] = make_float4(tv[0], tv[1], tv[2], tv[3]);
+          part_ti[(int64_t)g * N + n] = make_int4(ti[0], ti[1], ti[2], ti[3]);
         }
       }
       ok = epi_sync_and(ok);
@@ -448,46 +447,46 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, 2 * NC);
   }
 }
 
 // ------------------------------------------------------------------------- refine
-// Exact re-evaluation of each point's two leading components.  The tensor-core
-// log-likelihoods carry an absolute error of ~1e-4..1e-3 (the expanded form's terms
-// |x|^2/var are far larger than the Mahalanobis distance they cancel down to), while
-// responsibility mass sits on one or two components per point.  This kernel merges the
-// pass-1 partials of the component groups, recomputes the two leading log-likelihoods in
-// the direct form of flash_gmm/csrc/flash_gmm_cpu.cpp:30-45 (fp32, with
-// w = x var^{-1/2} - mu var^{-1/2} formed by one FMA), swaps them into the log-sum-exp,
-// and writes the log-normalizer (output and log2 form for pass 2), the two exact
-// log2-likelihoods over their tensor-core values in L, and one log-normalizer sum per
-// block.
-// Eight lanes per point (four points per warp), lanes striped over the dimensions; all
-// loads of a point are issued before its reductions.
-// Blocks per SM (register budget): five for 16 dimensions per lane, four below (measured).
-template <int DPL, bool VEC>  // dimensions per lane: ceil(d / 8); VEC: float4 loads
-__global__ void __launch_bounds__(256, DPL >= 16 ? 5 : 4)
+// Exact re-evaluation of each point's leading components.  The tensor-core
+// log-likelihoods carry an absolute error of ~1e-4 (the products are fp16 hi/lo pairs
+// and tensor-memory accumulation truncates), while the responsibility mass of a point
+// sits on its few leading components.  This kernel merges the pass-1 summaries of the
+// component groups and re-evaluates every one of the four leading log-likelihoods that
+// lies within 2^-kNear of the leader: sum_j ((x_j - mu_j) var_j^-1/2)^2 from the fp32
+// inputs, evaluated and summed in fp64 (the direct form of
+// flash_gmm/csrc/flash_gmm_cpu.cpp:30-45, which the reference evaluates in fp32).  The point's log-normalizer is formed in fp64 from them and the rest's sum.
+// Outputs per point: the log-normalizer (fp32 output, a fp64 block sum, and its base-2
+// form for the statistics pass), and the re-evaluated components with their base-2
+// log-responsibilities l2 - ln2 (fp32 of the fp64 difference: these small numbers keep
+// full precision, where an fp32 l2 of magnitude ~300 would not), which the statistics
+// pass substitutes for its tensor-core values.
+// Eight lanes per point (four points per warp), lanes striped over the dimensions; the
+// point's row is loaded first so its latency overlaps the partial loads.
+template <int DPL, bool VEC>  // dimensions per lane: ceil(d / 8); VEC: vector loads
+__global__ void __launch_bounds__(256, 4)
 tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__restrict__ sc,
-                 const float *__restrict__ ms, const float *__restrict__ lc,
+                 const float *__restrict__ mu, const double *__restrict__ lc,
                  const float *__restrict__ part_m, const float *__restrict__ part_s,
-                 const float2 *__restrict__ part_tv, const int2 *__restrict__ part_ti, int G,
-                 float *__restrict__ ln2x, float *__restrict__ Lt, int64_t Npad,
+                 const float4 *__restrict__ part_tv, const int4 *__restrict__ part_ti, int G,
+                 float *__restrict__ ln2x, int4 *__restrict__ top_i, float4 *__restrict__ top_d,
                  float *__restrict__ ln_out, double *__restrict__ ln_part, int acc_ln) {
   __shared__ double wsum[8];
   griddep_launch();
   griddep_wait();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int sub = lane & 7;           // lane within the point's group of 8
+  const int sub = lane & 7;  // lane within the point's group of 8
   double acc = 0.0;
   const int64_t stride = (int64_t)gridDim.x * 32;  // points per grid sweep
   for (int64_t n = ((int64_t)blockIdx.x * 8 + warp) * 4 + (lane >> 3); n - (lane >> 3) < N;
        n += stride) {
     const bool live = n < N;
     const int64_t nn = live ? n : 0;
-    // the point's row first (independent of everything below), so its latency overlaps
-    // the partial loads and the parameter gathers
-    float x[DPL], s1[DPL], m1[DPL], s2[DPL], m2[DPL];
+    float x[DPL];
     if (VEC) {  // d == 8 DPL, DPL % 4 == 0, 16-byte aligned rows; lane takes float4 i * 8 + sub
       const float4 *xp = reinterpret_cast<const float4 *>(X + nn * d) + sub;
 #pragma unroll
@@ -502,93 +501,77 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
         x[i] = j < d ? __ldg(X + nn * d + j) : 0.0f;
       }
     }
-    // merge the component groups' partials: online log-sum-exp and top-2
-    float mx = -INFINITY, sm = 0.0f, b1 = -INFINITY, b2 = -INFINITY;
-    int j1 = -1, j2 = -1;
-#pragma unroll 4
+    // merge the component groups' summaries: leading four and the log-sum-exp of the rest
+    float mx = -INFINITY, sm = 0.0f;
+    float b[kTcTop] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    int jx[kTcTop] = {-1, -1, -1, -1};
+#pragma unroll 2
     for (int g = 0; g < G; ++g) {
-      const float pm = __ldg(part_m + (int64_t)g * N + nn);
-      const float ps = __ldg(part_s + (int64_t)g * N + nn);
-      const float2 tv = part_tv[(int64_t)g * N + nn];
-      const int2 ti = part_ti[(int64_t)g * N + nn];
-      const float mn = fmaxf(mx, pm);
-      const float mr = mn == -INFINITY ? 0.0f : mn;
-      sm = sm * ex2(mx - mr) + ps * ex2(pm - mr);
-      mx = mn;
-      if (ti.x >= 0 && tv.x > b2) {
-        if (tv.x > b1) { b2 = b1; j2 = j1; b1 = tv.x; j1 = ti.x; }
-        else           { b2 = tv.x; j2 = ti.x; }
-      }
-      if (ti.y >= 0 && tv.y > b2) {
-        if (tv.y > b1) { b2 = b1; j2 = j1; b1 = tv.y; j1 = ti.y; }
-        else           { b2 = tv.y; j2 = ti.y; }
-      }
+      const float4 tv = __ldg(part_tv + (int64_t)g * N + nn);
+      const int4 ti = __ldg(part_ti + (int64_t)g * N + nn);
+      lse_merge(mx, sm, __ldg(part_m + (int64_t)g * N + nn), __ldg(part_s + (int64_t)g * N + nn));
+      if (ti.x >= 0) summary_push(b, jx, mx, sm, tv.x, ti.x);
+      if (ti.y >= 0) summary_push(b, jx, mx, sm, tv.y, ti.y);
+      if (ti.z >= 0) summary_push(b, jx, mx, sm, tv.z, ti.z);
+      if (ti.w >= 0) summary_push(b, jx, mx, sm, tv.w, ti.w);
     }
-    // the runner-up only matters when it is within 2^-40 of the leader (otherwise its
-    // responsibility is below 1e-12 and its tensor-core value is kept)
-    if (j2 >= 0 && b2 < b1 - 40.0f) j2 = -1;
-    const int k1 = j1 >= 0 ? j1 : 0, k2 = j2 >= 0 ? j2 : 0;
-    const bool need2 = __any_sync(0xffffffffu, j2 >= 0);
-    // the 8 lanes of a point read each row in consecutive 16-byte (VEC) or 4-byte pieces,
-    // so a load instruction of the warp touches whole 128-byte lines
-    const bool use2 = need2 && j2 >= 0;
-    if (VEC) {
-      const float4 *s1p = reinterpret_cast<const float4 *>(sc + (int64_t)k1 * d) + sub;
-      const float4 *m1p = reinterpret_cast<const float4 *>(ms + (int64_t)k1 * d) + sub;
-      const float4 *s2p = reinterpret_cast<const float4 *>(sc + (int64_t)k2 * d) + sub;
-      const float4 *m2p = reinterpret_cast<const float4 *>(ms + (int64_t)k2 * d) + sub;
+    // the components within 2^-kNear of the leader are re-evaluated (the others carry
+    // responsibilities below 2e-10 of the leader's and keep their tensor-core values)
+    double v[kTcTop];
+    bool ex[kTcTop];
 #pragma unroll
-      for (int i = 0; i < DPL / 4; ++i) {
-        const float4 b = __ldg(s1p + 8 * i), c = __ldg(m1p + 8 * i);
-        const float4 e = use2 ? __ldg(s2p + 8 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
-        const float4 f = use2 ? __ldg(m2p + 8 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
-        s1[4 * i] = b.x; s1[4 * i + 1] = b.y; s1[4 * i + 2] = b.z; s1[4 * i + 3] = b.w;
-        m1[4 * i] = c.x; m1[4 * i + 1] = c.y; m1[4 * i + 2] = c.z; m1[4 * i + 3] = c.w;
-        s2[4 * i] = e.x; s2[4 * i + 1] = e.y; s2[4 * i + 2] = e.z; s2[4 * i + 3] = e.w;
-        m2[4 * i] = f.x; m2[4 * i + 1] = f.y; m2[4 * i + 2] = f.z; m2[4 * i + 3] = f.w;
+    for (int c = 0; c < kTcTop; ++c) {
+      const bool need = jx[c] >= 0 && b[c] >= b[0] - kNear;
+      ex[c] = need;
+      v[c] = jx[c] >= 0 ? (double)b[c] : -INFINITY;
+      if (!__any_sync(0xffffffffu, need)) continue;
+      const int64_t kc = need ? jx[c] : 0;
+      double p = 0.0;
+      if (VEC) {
+#pragma unroll
+        for (int i = 0; i < DPL / 4; ++i) {
+          const int64_t q = kc * d + (int64_t)(i * 8 + sub) * 4;
+          const float4 m4 = need ? __ldg(reinterpret_cast<const float4 *>(mu + q)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float4 s4 = need ? __ldg(reinterpret_cast<const float4 *>(sc + q)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          // fp64 difference and scale (fp32 here leaves ~10x the error in the variances)
+          const double t0 = ((double)x[4 * i] - m4.x) * (double)s4.x;
+          const double t1 = ((double)x[4 * i + 1] - m4.y) * (double)s4.y;
+          const double t2 = ((double)x[4 * i + 2] - m4.z) * (double)s4.z;
+          const double t3 = ((double)x[4 * i + 3] - m4.w) * (double)s4.w;
+          p = fma(t0, t0, p); p = fma(t1, t1, p); p = fma(t2, t2, p); p = fma(t3, t3, p);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) {
+          const int j = i * 8 + sub;
+          const bool in = need && j < d;
+          const float s1 = in ? __ldg(sc + kc * d + j) : 0.0f;
+          const float m1 = in ? __ldg(mu + kc * d + j) : 0.0f;
+          const double t = ((double)x[i] - m1) * (double)s1;
+          p = fma(t, t, p);
+        }
       }
-    } else {
 #pragma unroll
-      for (int i = 0; i < DPL; ++i) {
-        const int j = i * 8 + sub;
-        const bool in = j < d;
-        s1[i] = in ? __ldg(sc + (int64_t)k1 * d + j) : 0.0f;
-        m1[i] = in ? __ldg(ms + (int64_t)k1 * d + j) : 0.0f;
-        s2[i] = in && use2 ? __ldg(sc + (int64_t)k2 * d + j) : 0.0f;
-        m2[i] = in && use2 ? __ldg(ms + (int64_t)k2 * d + j) : 0.0f;
-      }
+      for (int o = 4; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
+      if (need) v[c] = (__ldg(lc + kc) - 0.5 * p) * 1.4426950408889634;
     }
-    float p1 = 0.0f, p2 = 0.0f;
+    // the sum in fp64: the rest (fp32 tensor-core values), plus the leading four
+    double m = (double)mx;
 #pragma unroll
-    for (int i = 0; i < DPL; ++i) {
-      const float w1 = fmaf(x[i], s1[i], -m1[i]);
-      const float w2 = fmaf(x[i], s2[i], -m2[i]);
-      p1 = fmaf(w1, w1, p1);
-      p2 = fmaf(w2, w2, p2);
-    }
+    for (int c = 0; c < kTcTop; ++c) m = fmax(m, v[c]);
+    const double mr = m == -INFINITY ? 0.0 : m;
+    double tot = (double)sm * exp2((double)mx - mr);
 #pragma unroll
-    for (int o = 4; o > 0; o >>= 1) {
-      p1 += __shfl_xor_sync(0xffffffffu, p1, o);
-      p2 += __shfl_xor_sync(0xffffffffu, p2, o);
-    }
-    const float e1 = j1 >= 0 ? (__ldg(lc + k1) - 0.5f * p1) * kLog2e : -INFINITY;
-    const float e2 = j2 >= 0 ? (__ldg(lc + k2) - 0.5f * p2) * kLog2e : -INFINITY;
-    // swap the approximate leading terms of the sum for the exact ones
-    const float m = fmaxf(mx, fmaxf(e1, e2));
-    float rest = sm * ex2(mx - m);
-    if (j1 >= 0) rest -= ex2(b1 - m);
-    if (j2 >= 0) rest -= ex2(b2 - m);
-    float tot = fmaxf(rest, 0.0f);
-    if (j1 >= 0) tot += ex2(e1 - m);
-    if (j2 >= 0) tot += ex2(e2 - m);
-    const float ln2 = m + __log2f(tot);
+    for (int c = 0; c < kTcTop; ++c) tot += exp2(v[c] - mr);
+    const double ln2 = mr + log2(tot);
     if (live && sub == 0) {
-      ln2x[n] = ln2;
-      if (j1 >= 0) Lt[(int64_t)j1 * Npad + n] = e1;
-      if (j2 >= 0) Lt[(int64_t)j2 * Npad + n] = e2;
-      const float l = ln2 * kLn2;
-      ln_out[n] = l;
-      acc += (double)l;
+      ln2x[n] = (float)ln2;
+      top_i[n] = make_int4(ex[0] ? jx[0] : -1, ex[1] ? jx[1] : -1, ex[2] ? jx[2] : -1, ex[3] ? jx[3] : -1);
+      top_d[n] = make_float4((float)(v[0] - ln2), (float)(v[1] - ln2), (float)(v[2] - ln2),
+                             (float)(v[3] - ln2));
+      const double l = ln2 * 0.6931471805599453;
+      ln_out[n] = (float)l;
+      acc += l;
     }
   }
 #pragma unroll
@@ -603,42 +586,42 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
 }
 
 // ------------------------------------------------------------------------- pass 2
-// Statistics GEMM S[k, f] = sum_n gamma[n, k] F[n, f] with F = [x^2 | x] (3xTF32), the
-// only tensor-core work left once pass 1 has stored the log2-likelihood matrix L (with
-// the refined leading components written over their tensor-core values).  A CTA owns
-// 128 components (the M of the MMA, on the TMEM lanes) and a contiguous range of points,
-// taken in slices of 16 points (the K of two MMA k-steps).  Warp roles (16 warps):
-//   warp 9 lane 0 (producer): per slice, TMA of F hi and F lo from the prepared points
-//     buffer (one 3-D box each: 16 points x all 32-feature atoms, MN-major
-//     SWIZZLE_128B_ATOM_32B), of the slice's L tile [16 points][128 components] and of
-//     its 16 log2-normalizers, into a ring of kStages slices;
-//   warps 0-7 (gamma): warp w computes gamma = 2^(L - ln2) for components
-//     32 (w % 4) .. +31 (its TMEM lane quarter) at 8 of the slice's 16 points, splits it
-//     into tf32 hi / lo and stores both to a TMEM gamma buffer (ring of kGBufs), the
-//     MMA's A operand;
-//   warp 8 lane 0 (MMA): six MMAs per slice (gamma_lo F_hi, gamma_hi F_lo, then
-//     gamma_hi F_hi, two k-steps each) into the statistics accumulator;
+// Statistics GEMM S[k, f] = sum_n gamma[n, k] F[n, f] with F = [x^2 | x] (fp16 hi/lo,
+// column-scaled), the tensor-core work left once pass 1 has stored the log2-likelihood
+// block Lt (with the exact leading components written over their tensor-core values).
+// A CTA owns 128 components (the M of the MMA, on the TMEM lanes) and a contiguous range
+// of points, taken in slices of 16 points (the K of one kind::f16 k-step).  Roles:
+//   warp 9 lane 0 (producer): per slice, TMA of F hi and F lo (one 3-D box each: 16 points
+//     x all 64-feature atoms, MN-major SWIZZLE_128B), of the slice's Lt tile
+//     [16 points][128 components] and of its 16 log2-normalizers;
+//   warps 0-7 (gamma): warp w computes gamma = 2^(l2 - ln2) for components 32 (w % 4) ..
+//     +31 (its TMEM lane quarter) at 8 of the slice's 16 points, scales it by 2^14,
+//     splits it into fp16 hi / lo and stores the pairs into a TMEM gamma buffer (two
+//     points per 32-bit column), the MMA's A operand;
+//   warp 8 lane 0 (MMA): three MMAs per slice (gamma_lo F_hi, gamma_hi F_lo, gamma_hi
+//     F_hi) into the statistics accumulator;
 //   all 16 warps: every kSlicesFlush slices (128 points) the accumulator is added into
 //     fp32 registers (warp w: lane quarter w % 4, a quarter of the columns), because
-//     tensor-memory accumulation does not round to nearest.  With two accumulator
-//     regions (KA <= 192) the tensor pipe fills one while the other drains; at KA = 256
-//     the single region is drained between tiles.  Warps waiting only for a drain sleep
-//     between polls.
+//     tensor-memory accumulation does not round to nearest.  With two accumulator regions
+//     (KA <= 192) the tensor pipe fills one while the other drains.
 // Every hand-off is an mbarrier; no barrier spans the CTA inside the loop.
-constexpr int kSlicePts = 16;
-constexpr int kSlicesFlush = 8;
+constexpr int kSlicePts = 32;
+constexpr int kSlicesFlush = 4;
 constexpr int kGBufs = 4;
 constexpr int kThreads2 = 512;
 constexpr int kGammaWarps = 8;
-constexpr int kGCols = 2 * kSlicePts;  // TMEM columns of one gamma buffer (hi | lo)
+constexpr int kGPts = kSlicePts / 2;  // points of a slice per gamma warp
+constexpr int kGCols = kSlicePts;     // TMEM columns of one gamma buffer: hi 16 | lo 16
+constexpr int NC2 = 128;    // components per statistics CTA
 
 template <int KA>
 struct StatsShape {
-  static constexpr int kAtom = kSlicePts * 128;                // 2 KB: 16 points x 32 fp32
-  static constexpr int kFPart = (KA / 32) * kAtom;             // F hi (or lo) of a slice
-  static constexpr int kLOff = 2 * kFPart;                     // L tile [128][16], 64B-swizzled
-  static constexpr int kNOff = kLOff + kSlicePts * NC * 4;     // ln2 [16]
-  static constexpr int kStage = (kNOff + kSlicePts * 4 + 1023) / 1024 * 1024;
+  static constexpr int kAtom = kSlicePts * 128;                // 4 KB: 32 points x 64 fp16
+  static constexpr int kFPart = (KA / 64) * kAtom;             // F hi (or lo) of a slice
+  static constexpr int kLOff = 2 * kFPart;                     // Lt tile [128][32], 128B-swizzled
+  static constexpr int kNOff = kLOff + kSlicePts * NC2 * 4;    // ln2 [32]
+  static constexpr int kTOff = kNOff + kSlicePts * 4;          // exact leaders: int4 [32], float4 [32]
+  static constexpr int kStage = (kTOff + kSlicePts * 32 + 1023) / 1024 * 1024;
   static constexpr int kStagesFit = (220 * 1024) / kStage;
   static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
   static constexpr int kSmem = 1024 + kStages * kStage + 512;
@@ -648,14 +631,21 @@ __device__ __forceinline__ bool cta_sync_and(bool v) {
   return __syncthreads_and(v ? 1 : 0) != 0;
 }
 
+// Two fp16 K elements in one 32-bit TMEM column: the lower K index in the low half.
+__device__ __forceinline__ uint32_t pack_half2(__half lo_k, __half hi_k) {
+  return (uint32_t)__half_as_ushort(lo_k) | ((uint32_t)__half_as_ushort(hi_k) << 16);
+}
+
 // Partial statistics row (per component and CTA slot, partial[k][slot]):
-// [s (DP) | sq (DP) | n | pad], stride 2 DP + 4.
-template <int NKC>
+// [s (DP) | sq (DP) | n | pad], stride 2 DP + 4, unscaled fp32.
+template <int NKCF>
 __global__ void __launch_bounds__(kThreads2, 1)
 tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constant__ CUtensorMap tm_flo,
-                const __grid_constant__ CUtensorMap tm_l, const float *__restrict__ ln2x, int64_t N,
-                int S_slots, int K, float *__restrict__ partial, int accum) {
-  constexpr int KA = NKC * KC;
+                const __grid_constant__ CUtensorMap tm_l, const float *__restrict__ ln2x,
+                const int4 *__restrict__ top_i, const float4 *__restrict__ top_d, int64_t N,
+                int S_slots, int K, int d, const int *__restrict__ aexp, float *__restrict__ partial,
+                int accum) {
+  constexpr int KA = NKCF * 64;
   constexpr int DP = KA / 2;
   constexpr int PSTRIDE = 2 * DP + 4;
   constexpr int SEG = KA / 4;  // statistics columns per warp
@@ -751,7 +741,8 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
   float nk = 0.0f;
   if (warp < kGammaWarps) {
     // ---------------- gamma warps
-    const int p0 = (warp >> 2) * 8;  // this warp's 8 points of each slice
+    const int p0 = (warp >> 2) * kGPts;  // this warp's points of each slice
+    const float gscale = (float)(1 << kTcGammaExp);
     for (int s = 0; s < S && ok; ++s) {
       // Tile j is drained once this warp is kGBufs slices into tile j + 1: having waited
       // for the MMAs of slice 8j + 7 it finds tile j complete, and the drain comes before
@@ -764,16 +755,19 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
       if (!ok) break;
       tc_fence_after();
       const uint8_t *stg = smem + st * Sh::kStage;
-      // this lane's component row of the L tile: 16 points = four 16-byte chunks, chunk c
-      // stored at c ^ ((row >> 1) & 3) (SWIZZLE_64B)
-      const float4 *Lrow = reinterpret_cast<const float4 *>(stg + Sh::kLOff + cl * 64);
-      const int sw = (cl >> 1) & 3;
+      // this lane's component row of the Lt tile: 32 points = eight 16-byte chunks, chunk c
+      // stored at c ^ (row & 7) (SWIZZLE_128B)
+      const float4 *Lrow = reinterpret_cast<const float4 *>(stg + Sh::kLOff + cl * 128);
+      const int sw = cl & 7;
       const float4 *ln4 = reinterpret_cast<const float4 *>(stg + Sh::kNOff);
+      const int4 *ti_s = reinterpret_cast<const int4 *>(stg + Sh::kTOff);
+      const float4 *td_s = reinterpret_cast<const float4 *>(stg + Sh::kTOff + kSlicePts * 16);
+      const int kabs = ct * NC2 + cl;
       const int64_t nb = (s0 + s) * kSlicePts;
       const int live = (N - nb < kSlicePts ? (int)(N - nb) : kSlicePts) - p0;
-      float gh[8], gl[8];
+      __half gh[kGPts], gl[kGPts];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < kGPts / 4; ++c) {
         const float4 l4 = ln4[p0 / 4 + c];
         const float4 v4 = Lrow[(p0 / 4 + c) ^ sw];
         const float ln2[4] = {l4.x, l4.y, l4.z, l4.w};
@@ -781,17 +775,31 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int p = c * 4 + e;
-          const float g = p < live ? ex2(lv[e] - ln2[e]) : 0.0f;
+          // base-2 log-responsibility: the exact value for the point's re-evaluated
+          // leading components, else the tensor-core value
+          const int4 ti = ti_s[p0 + p];
+          const float4 td = td_s[p0 + p];
+          float dl = lv[e] - ln2[e];
+          dl = kabs == ti.x ? td.x : dl;
+          dl = kabs == ti.y ? td.y : dl;
+          dl = kabs == ti.z ? td.z : dl;
+          dl = kabs == ti.w ? td.w : dl;
+          const float g = p < live ? ex2(dl) : 0.0f;
           nk += g;
-          gh[p] = to_tf32(g);
-          gl[p] = to_tf32(g - gh[p]);
+          split_f16f(g * gscale, gh[p], gl[p]);
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(EMPTY(st));  // this warp is done with the slice's L
-      const uint32_t ga = lane_tmem + kGBase + gb * kGCols + p0;
-      tmem_st8(ga, gh);
-      tmem_st8(ga + kSlicePts, gl);
+      if (lane == 0) mbar_arrive(EMPTY(st));  // this warp is done with the slice's Lt
+      uint32_t hi8[kGPts / 2], lo8[kGPts / 2];
+#pragma unroll
+      for (int i = 0; i < kGPts / 2; ++i) {
+        hi8[i] = pack_half2(gh[2 * i], gh[2 * i + 1]);
+        lo8[i] = pack_half2(gl[2 * i], gl[2 * i + 1]);
+      }
+      const uint32_t ga = lane_tmem + kGBase + gb * kGCols + p0 / 2;
+      tmem_st8(ga, *reinterpret_cast<const float(*)[8]>(hi8));
+      tmem_st8(ga + kSlicePts / 2, *reinterpret_cast<const float(*)[8]>(lo8));
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -799,8 +807,9 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
     }
   } else if (warp == kGammaWarps) {
     // ---------------- MMA warp
-    constexpr uint32_t idesc = idesc_tf32(NC, KA, 0, 1);  // A from TMEM, B MN-major
-    const uint64_t fdesc0 = sdesc(smem_u32(smem), Sh::kAtom, 512, kSw128Base32);
+    constexpr uint32_t idesc = idesc_f16(NC2, KA, 0, 1);  // A from TMEM, B MN-major
+    // B: 64-feature atoms of kSlicePts points each: LBO = atom stride, SBO = 8 points (1 KB)
+    const uint64_t fdesc0 = sdesc(smem_u32(smem), Sh::kAtom, 1024, kSw128);
     for (int s = 0; s < S && ok; ++s) {
       const int j = s / kSlicesFlush, reg = NSR == 2 ? (j & 1) : 0;
       const bool tile_first = s % kSlicesFlush == 0;
@@ -816,16 +825,16 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
         tc_fence_after();
         const uint32_t gbuf = tmem + kGBase + gb * kGCols;
         const uint32_t dst = tmem + reg * KA;
-        // the stage's descriptor; F lo and the second k-step are fixed address offsets
         const uint64_t fd = fdesc0 + (uint64_t)((st * Sh::kStage) >> 4);
-        constexpr uint64_t kLo = Sh::kFPart >> 4, kK = 1024 >> 4;
+        constexpr uint64_t kLo = Sh::kFPart >> 4, kK = (16 * 128) >> 4;  // k-step: 16 points
+        constexpr uint32_t kGLo = kSlicePts / 2;                          // gamma lo columns
 #pragma unroll
-        for (int kk = 0; kk < 2; ++kk) {
-          mma_tf32_ta(dst, gbuf + kSlicePts + kk * 8, fd + kk * kK, idesc, (tile_first && kk == 0) ? 0u : 1u);
-          mma_tf32_ta(dst, gbuf + kk * 8, fd + kLo + kk * kK, idesc, 1u);
+        for (int kk = 0; kk < kSlicePts / 16; ++kk) {
+          mma_f16_ta(dst, gbuf + kGLo + kk * 8, fd + kk * kK, idesc, (tile_first && kk == 0) ? 0u : 1u);
+          mma_f16_ta(dst, gbuf + kk * 8, fd + kLo + kk * kK, idesc, 1u);
         }
 #pragma unroll
-        for (int kk = 0; kk < 2; ++kk) mma_tf32_ta(dst, gbuf + kk * 8, fd + kk * kK, idesc, 1u);
+        for (int kk = 0; kk < kSlicePts / 16; ++kk) mma_f16_ta(dst, gbuf + kk * 8, fd + kk * kK, idesc, 1u);
         mma_commit(EMPTY(st));
         mma_commit(GEMPTY(gb));
         if (s % kSlicesFlush == kSlicesFlush - 1 || s == S - 1) mma_commit(SFULL(reg));
@@ -844,7 +853,7 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
       prefetch_tmap(&tm_flo);
       prefetch_tmap(&tm_l);
     }
-    // L is read exactly once
+    // Lt is read exactly once
     const uint64_t pol_l = policy_evict_first();
     for (int s = 0; s < S && ok; ++s) {
       // same rule as the gamma warps, NST slices ahead (before the EMPTY wait below)
@@ -856,11 +865,13 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
       if (lane == 0) {
         const uint32_t base = smem_u32(smem + st * Sh::kStage);
         const int64_t nb = (s0 + s) * kSlicePts;
-        mbar_arrive_expect_tx(FULL(st), 2 * Sh::kFPart + kSlicePts * NC * 4 + kSlicePts * 4);
+        mbar_arrive_expect_tx(FULL(st), 2 * Sh::kFPart + kSlicePts * NC2 * 4 + kSlicePts * 36);  // F, Lt, ln2, leaders
         tma_load_3d(base, &tm_fhi, 0, (int32_t)nb, 0, FULL(st));
         tma_load_3d(base + Sh::kFPart, &tm_flo, 0, (int32_t)nb, 0, FULL(st));
-        tma_load_2d_hint(base + Sh::kLOff, &tm_l, (int32_t)nb, ct * NC, FULL(st), pol_l);
+        tma_load_2d_hint(base + Sh::kLOff, &tm_l, (int32_t)nb, ct * NC2, FULL(st), pol_l);
         bulk_load(base + Sh::kNOff, ln2x + nb, kSlicePts * 4, FULL(st));
+        bulk_load(base + Sh::kTOff, top_i + nb, kSlicePts * 16, FULL(st));
+        bulk_load(base + Sh::kTOff + kSlicePts * 16, top_d + nb, kSlicePts * 16, FULL(st));
       }
       __syncwarp();
     }
@@ -874,15 +885,20 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
   while (nf < T && ok) flush_next(warp > kGammaWarps + 1);
 
   ok = cta_sync_and(ok);
-  const int k = ct * NC + cl;
+  const int k = ct * NC2 + cl;
   if (k < K) {
     float *dst = partial + ((int64_t)k * S_slots + slot) * PSTRIDE;
 #pragma unroll
     for (int e = 0; e < SEG; e += 4) {
       const int f = seg * SEG + e;  // feature column: x^2 part first, then x
+      const int j0 = f < DP ? f : f - DP, t = f < DP ? 0 : 1;
+      float r[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)  // undo the column scale and the responsibility scale
+        r[i] = (ok && j0 + i < d) ? ldexpf(sacc[e + i], -(__ldg(aexp + 3 * (j0 + i) + t) + kTcGammaExp))
+                                  : 0.0f;
       float4 *o = reinterpret_cast<float4 *>(dst + (f < DP ? DP + f : f - DP));
-      float4 v = ok ? make_float4(sacc[e], sacc[e + 1], sacc[e + 2], sacc[e + 3])
-                    : make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 v = make_float4(r[0], r[1], r[2], r[3]);
       if (accum) {  // a later chunk of the same iteration: this CTA slot's row adds up
         const float4 o0 = *o;
         v = make_float4(o0.x + v.x, o0.y + v.y, o0.z + v.z, o0.w + v.w);
@@ -921,35 +937,35 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// Row-major fp32 [rows][cols] matrix, box [box_rows][box_cols] with the given swizzle.
-// Row-major fp32 [rows][cols] matrix (cols a multiple of 32) seen as 32-column atoms:
-// box = 32 rows x all atoms, landing as [atom][row][32] with SWIZZLE_128B_ATOM_32B (the
-// MN-major operand layout of the statistics GEMM).
-int make_map_atoms(CUtensorMap *m, const float *base, int64_t rows, int cols, int box_rows) {
+// Row-major fp16 [rows][cols] matrix (cols a multiple of 64) seen as 64-column atoms:
+// box = box_rows x all atoms, landing as [atom][row][64] with SWIZZLE_128B (the MN-major
+// operand layout of the statistics GEMM).
+int make_map_atoms16(CUtensorMap *m, const __half *base, int64_t rows, int cols, int box_rows) {
   auto fn = encode_fn();
   if (!fn) return fail(FGMM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[3] = {(cuuint64_t)KC, (cuuint64_t)rows, (cuuint64_t)(cols / KC)};
-  cuuint64_t strides[2] = {(cuuint64_t)cols * sizeof(float), (cuuint64_t)KC * sizeof(float)};
-  cuuint32_t box[3] = {(cuuint32_t)KC, (cuuint32_t)box_rows, (cuuint32_t)(cols / KC)};
+  cuuint64_t dims[3] = {(cuuint64_t)KCH, (cuuint64_t)rows, (cuuint64_t)(cols / KCH)};
+  cuuint64_t strides[2] = {(cuuint64_t)cols * 2, (cuuint64_t)KCH * 2};
+  cuuint32_t box[3] = {(cuuint32_t)KCH, (cuuint32_t)box_rows, (cuuint32_t)(cols / KCH)};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half *>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(FGMM_ERR_CUDA, "cuTensorMapEncodeTiled (atoms) failed: " + std::to_string((int)r));
   return FGMM_OK;
 }
 
-int make_map(CUtensorMap *m, const float *base, int64_t rows, int cols, int box_rows,
-             CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B, int box_cols = KC) {
+// Row-major [rows][cols] matrix of `dtype` (element size `es`), box [box_rows][box_cols].
+int make_map(CUtensorMap *m, const void *base, CUtensorMapDataType dtype, int es, int64_t rows,
+             int64_t cols, int box_rows, int box_cols, CUtensorMapSwizzle swz) {
   auto fn = encode_fn();
   if (!fn) return fail(FGMM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)cols * sizeof(float)};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * es};
   cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(m, dtype, 2, const_cast<void *>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(FGMM_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
   return FGMM_OK;
 }
@@ -958,10 +974,7 @@ int make_map(CUtensorMap *m, const float *base, int64_t rows, int cols, int box_
 // fixed budget, so the workspace stays bounded for any N: pass 1 writes the block, the
 // refine kernel patches it and the statistics kernel reads it back.  Chunks run in order
 // on the stream; the per-slot statistics rows and the log-normalizer block sums add up
-// across chunks.  The budget (256 MB, twice the L2) is set by the per-chunk cost of three
-// launches and their pipeline fill and drain, which outweighs keeping the block
-// L2-resident: against 64 MB, config 4 (K = 1024) runs 21 % and config 5 13 % faster;
-// larger budgets measured no further change.
+// across chunks.
 #ifndef FGMM_L_CHUNK_MB
 #define FGMM_L_CHUNK_MB 256
 #endif
@@ -975,11 +988,11 @@ struct TcChunk {
 
 struct TcPlan {
   int64_t N, Nc;  // all points; points per chunk (a multiple of 128, the last may be short)
-  int d, dp, KA, nkc, K, Kp, n_ct, chunks;
+  int d, dp, KA, kbp, nkc, nkcf, K, NC, Kp, n_ct, n_ct2, chunks;
   TcChunk first;
 };
 
-TcChunk chunk_plan(int64_t Nc, int n_ct) {
+TcChunk chunk_plan(int64_t Nc, int n_ct, int n_ct2) {
   TcChunk c{};
   c.Nc = Nc;
   c.n_pt = (int)cdiv(Nc, BM);
@@ -988,30 +1001,40 @@ TcChunk chunk_plan(int64_t Nc, int n_ct) {
   c.tpg = (int)cdiv(n_ct, G);
   c.G = (int)cdiv(n_ct, c.tpg);
   c.grid1 = (int)std::min<int64_t>((int64_t)c.n_pt * c.G, sms);
-  c.S = (int)std::max<int64_t>(1, std::min<int64_t>(sms / std::max(1, n_ct), cdiv(Nc, 32)));
-  c.grid2 = n_ct * c.S;
+  c.S = (int)std::max<int64_t>(1, std::min<int64_t>(sms / std::max(1, n_ct2), cdiv(Nc, 32)));
+  c.grid2 = n_ct2 * c.S;
   return c;
 }
 
 TcPlan plan(int64_t N, int d, int K) {
   TcPlan p{};
   p.N = N; p.d = d; p.K = K;
-  p.dp = dp_of(d);
+  p.dp = tc_dp(d);
   p.KA = 2 * p.dp;
-  p.nkc = p.KA / KC;
-  p.n_ct = (int)cdiv(K, NC);
-  p.Kp = p.n_ct * NC;
+  p.kbp = tc_kbp(d);
+  p.nkc = p.kbp / KCH;
+  p.nkcf = p.KA / KCH;
+#ifdef FGMM_PASS1_NC128
+  p.NC = 128;
+#else
+  p.NC = K <= 128 ? 128 : 256;
+#endif
+  p.n_ct = (int)cdiv(K, p.NC);
+  p.Kp = p.n_ct * p.NC;
+  p.n_ct2 = (int)cdiv(K, NC2);
   const int64_t fit = std::max<int64_t>(BM, kLChunkBytes / ((int64_t)p.Kp * 4) / BM * BM);
   p.Nc = std::min<int64_t>(npad_of(N), fit);
   p.chunks = (int)cdiv(N, p.Nc);
-  p.first = chunk_plan(std::min<int64_t>(N, p.Nc), p.n_ct);
+  p.first = chunk_plan(std::min<int64_t>(N, p.Nc), p.n_ct, p.n_ct2);
   return p;
 }
 
 struct TcWs {
-  float *qhi, *qlo, *cst2, *sc, *ms, *lc, *part_m, *part_s, *ln2x, *partial, *L;
-  float2 *part_tv;
-  int2 *part_ti;
+  __half *qhi, *qlo;
+  float *coef, *cst2, *sc, *mu, *part_m, *part_s, *ln2x, *partial, *L;
+  double *lc;
+  float4 *part_tv, *top_d;
+  int4 *part_ti, *top_i;
   double *ln_part;
   size_t bytes;
 };
@@ -1025,17 +1048,20 @@ TcWs tc_layout(void *ws, const TcPlan &p) {
   TcWs w{};
   Carve c(ws);
   const int64_t Nc = p.first.Nc;
-  w.qhi = c.take<float>((size_t)p.Kp * p.KA);
-  w.qlo = c.take<float>((size_t)p.Kp * p.KA);
+  w.qhi = c.take<__half>((size_t)p.Kp * p.kbp);
+  w.qlo = c.take<__half>((size_t)p.Kp * p.kbp);
+  w.coef = c.take<float>(p.Kp);
   w.cst2 = c.take<float>(p.Kp);
   w.sc = c.take<float>((size_t)p.K * p.d);
-  w.ms = c.take<float>((size_t)p.K * p.d);
-  w.lc = c.take<float>(p.K);
+  w.mu = c.take<float>((size_t)p.K * p.d);
+  w.lc = c.take<double>(p.K);
   w.part_m = c.take<float>((size_t)p.n_ct * Nc);
   w.part_s = c.take<float>((size_t)p.n_ct * Nc);
-  w.part_tv = c.take<float2>((size_t)p.n_ct * Nc);
-  w.part_ti = c.take<int2>((size_t)p.n_ct * Nc);
+  w.part_tv = c.take<float4>((size_t)p.n_ct * Nc);
+  w.part_ti = c.take<int4>((size_t)p.n_ct * Nc);
   w.ln2x = c.take<float>(npad_of(Nc));
+  w.top_i = c.take<int4>(npad_of(Nc));
+  w.top_d = c.take<float4>(npad_of(Nc));
   w.partial = c.take<float>((size_t)p.first.S * p.K * (2 * p.dp + 4));
   w.ln_part = c.take<double>(kRefineBlocks);
   w.L = c.take<float>((size_t)npad_of(Nc) * p.Kp);  // Lt [Kp][chunk]
@@ -1043,36 +1069,95 @@ TcWs tc_layout(void *ws, const TcPlan &p) {
   return w;
 }
 
-size_t smem1_bytes() { return 1024 + kStages1 * kStageBytes + 256 + (kParts - 1) * BM * 24; }
-size_t smem2_bytes(int KA) {
-  switch (KA) {
-    case 64: return StatsShape<64>::kSmem;
-    case 128: return StatsShape<128>::kSmem;
-    case 192: return StatsShape<192>::kSmem;
-    default: return StatsShape<256>::kSmem;
+TcParamOps param_ops(const TcWs &w, const TcPlan &p, const void *points) {
+  TcParamOps op;
+  op.qhi = w.qhi; op.qlo = w.qlo; op.coef = w.coef; op.cst2 = w.cst2;
+  op.sc = w.sc; op.mu = w.mu; op.lc = w.lc;
+  op.aexp = pts_ptrs(points, p.N, p.d).aexp;
+  op.kbp = p.kbp;
+  return op;
+}
+
+// Kernel attributes are per device and per kernel: `Tag` (one type per kernel
+// instantiation) keeps one flag per device.
+template <typename Tag, typename F>
+int set_smem_once(F *kernel, int bytes) {
+  static std::atomic<bool> done[64];
+  int dev = 0;
+  FGMM_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!done[dev].load(std::memory_order_acquire)) {
+    FGMM_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done[dev].store(true, std::memory_order_release);
   }
+  return FGMM_OK;
+}
+
+template <int NKC, int NC>
+int launch_pass1(const TcPlan &p, const TcChunk &c, const PtsPtrs &pp, int64_t n0, const TcWs &w,
+                 cudaStream_t st) {
+  using Sh = Pass1Shape<NKC, NC>;
+  int rc = set_smem_once<Sh>(tc_pass1_kernel<NKC, NC>, Sh::kSmem);
+  if (rc) return rc;
+  const int64_t rows = npad_of(c.Nc);
+  CUtensorMap m_phi, m_plo, m_qhi, m_qlo;
+  const auto F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
+  if ((rc = make_map(&m_phi, pp.phi + n0 * p.kbp, F16, 2, rows, p.kbp, BM, KCH, SW))) return rc;
+  if ((rc = make_map(&m_plo, pp.plo + n0 * p.kbp, F16, 2, rows, p.kbp, BM, KCH, SW))) return rc;
+  if ((rc = make_map(&m_qhi, w.qhi, F16, 2, p.Kp, p.kbp, NC, KCH, SW))) return rc;
+  if ((rc = make_map(&m_qlo, w.qlo, F16, 2, p.Kp, p.kbp, NC, KCH, SW))) return rc;
+  FGMM_CUDA_TRY(launch_pdl(tc_pass1_kernel<NKC, NC>, c.grid1, kThreads1, Sh::kSmem, st, m_phi, m_plo,
+                           m_qhi, m_qlo, w.coef, w.cst2, c.Nc, c.n_pt, p.n_ct, c.G, c.tpg, w.part_m,
+                           w.part_s, w.part_tv, w.part_ti, w.L, rows));
+  mark(st, "tc_pass1_kernel");
+  return FGMM_OK;
+}
+
+template <int NKC>
+int launch_pass1_nc(const TcPlan &p, const TcChunk &c, const PtsPtrs &pp, int64_t n0, const TcWs &w,
+                    cudaStream_t st) {
+  return p.NC == 128 ? launch_pass1<NKC, 128>(p, c, pp, n0, w, st)
+                     : launch_pass1<NKC, 256>(p, c, pp, n0, w, st);
+}
+
+template <int NKCF>
+int launch_stats(const TcPlan &p, const TcChunk &c, const PtsPtrs &pp, int64_t n0, const TcWs &w,
+                 bool first, cudaStream_t st) {
+  constexpr int KA = NKCF * 64;
+  int rc = set_smem_once<StatsShape<KA>>(tc_stats_kernel<NKCF>, (int)StatsShape<KA>::kSmem);
+  if (rc) return rc;
+  const int64_t rows = npad_of(c.Nc);
+  CUtensorMap m_fhi, m_flo, m_l;
+  if ((rc = make_map_atoms16(&m_fhi, pp.fhi + n0 * p.KA, rows, p.KA, kSlicePts))) return rc;
+  if ((rc = make_map_atoms16(&m_flo, pp.flo + n0 * p.KA, rows, p.KA, kSlicePts))) return rc;
+  if ((rc = make_map(&m_l, w.L, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.Kp, rows, NC2, kSlicePts,
+                     CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  FGMM_CUDA_TRY(launch_pdl(tc_stats_kernel<NKCF>, c.grid2, kThreads2, StatsShape<KA>::kSmem, st,
+                           m_fhi, m_flo, m_l, w.ln2x, w.top_i, w.top_d, c.Nc, c.S, p.K, p.d, pp.aexp,
+                           w.partial,
+                           first ? 0 : 1));
+  mark(st, "tc_stats_kernel");
+  return FGMM_OK;
 }
 
 // Pass 1, refine and statistics for the chunk of points [n0, n0 + c.Nc).
-template <int NKC>
 int tc_launch_chunk(const TcPlan &p, const TcChunk &c, int64_t n0, bool first, const float *X,
-                    const float *pts, const TcWs &w, float *ln, cudaStream_t st) {
-  const float *phi = pts + n0 * p.KA;
-  const float *plo = pts + points_half_floats(p.N, p.d) + n0 * p.KA;
-  const int64_t rows = npad_of(c.Nc);
-  const int64_t lcols = npad_of(c.Nc);
-  const float *Xc = X + n0 * p.d;
-  CUtensorMap m_phi, m_plo, m_qhi, m_qlo;
+                    const PtsPtrs &pp, const TcWs &w, float *ln, cudaStream_t st) {
   int rc;
-  if ((rc = make_map(&m_phi, phi, rows, p.KA, BM))) return rc;
-  if ((rc = make_map(&m_plo, plo, rows, p.KA, BM))) return rc;
-  if ((rc = make_map(&m_qhi, w.qhi, p.Kp, p.KA, NC))) return rc;
-  if ((rc = make_map(&m_qlo, w.qlo, p.Kp, p.KA, NC))) return rc;
-  FGMM_CUDA_TRY(launch_pdl(tc_pass1_kernel<NKC>, c.grid1, kThreads, smem1_bytes(), st, m_phi, m_plo,
-                           m_qhi, m_qlo, w.cst2, c.Nc, c.n_pt, p.n_ct, c.G, c.tpg, w.part_m,
-                           w.part_s, w.part_tv, w.part_ti, w.L, lcols));
-  mark(st, "tc_pass1_kernel");
+  switch (p.nkc) {
+    case 1: rc = launch_pass1_nc<1>(p, c, pp, n0, w, st); break;
+    case 2: rc = launch_pass1_nc<2>(p, c, pp, n0, w, st); break;
+    case 3: rc = launch_pass1_nc<3>(p, c, pp, n0, w, st); break;
+    case 4: rc = launch_pass1_nc<4>(p, c, pp, n0, w, st); break;
+    case 5: rc = launch_pass1_nc<5>(p, c, pp, n0, w, st); break;
+    case 6: rc = launch_pass1_nc<6>(p, c, pp, n0, w, st); break;
+    default: return fail(FGMM_ERR_UNSUPPORTED, "tcgen05 family: d > 128");
+  }
+  if (rc) return rc;
   {
+    const float *Xc = X + n0 * p.d;
     const int blocks = refine_blocks(c.Nc);
     const int dpl = (p.d + 7) / 8;
     const bool vec = p.d % 32 == 0 && reinterpret_cast<uintptr_t>(Xc) % 16 == 0;  // d = 8 DPL
@@ -1081,12 +1166,12 @@ int tc_launch_chunk(const TcPlan &p, const TcChunk &c, int64_t n0, bool first, c
   do {                                                                                             \
     if (vec && (D) % 4 == 0 && 8 * (D) == p.d)                                                     \
       FGMM_CUDA_TRY(launch_pdl(tc_refine_kernel<D, true>, blocks, 256, 0, st, Xc, c.Nc, p.d, w.sc, \
-                               w.ms, w.lc, w.part_m, w.part_s, w.part_tv, w.part_ti, c.G, w.ln2x,  \
-                               w.L, lcols, ln + n0, w.ln_part, acc));                              \
+                               w.mu, w.lc, w.part_m, w.part_s, w.part_tv, w.part_ti, c.G, w.ln2x,  \
+                               w.top_i, w.top_d, ln + n0, w.ln_part, acc));                        \
     else                                                                                           \
       FGMM_CUDA_TRY(launch_pdl(tc_refine_kernel<D, false>, blocks, 256, 0, st, Xc, c.Nc, p.d, w.sc,\
-                               w.ms, w.lc, w.part_m, w.part_s, w.part_tv, w.part_ti, c.G, w.ln2x,  \
-                               w.L, lcols, ln + n0, w.ln_part, acc));                              \
+                               w.mu, w.lc, w.part_m, w.part_s, w.part_tv, w.part_ti, c.G, w.ln2x,  \
+                               w.top_i, w.top_d, ln + n0, w.ln_part, acc));                        \
   } while (0)
     if (dpl <= 1) FGMM_REFINE(1);
     else if (dpl <= 2) FGMM_REFINE(2);
@@ -1098,54 +1183,39 @@ int tc_launch_chunk(const TcPlan &p, const TcChunk &c, int64_t n0, bool first, c
     FGMM_LAUNCH_CHECK("tc_refine_kernel");
     mark(st, "tc_refine_kernel");
   }
-  CUtensorMap m_fhi, m_flo, m_l;
-  if ((rc = make_map_atoms(&m_fhi, phi, rows, p.KA, kSlicePts))) return rc;
-  if ((rc = make_map_atoms(&m_flo, plo, rows, p.KA, kSlicePts))) return rc;
-  if ((rc = make_map(&m_l, w.L, p.Kp, (int)lcols, NC, CU_TENSOR_MAP_SWIZZLE_64B, kSlicePts))) return rc;
-  FGMM_CUDA_TRY(launch_pdl(tc_stats_kernel<NKC>, c.grid2, kThreads2, smem2_bytes(NKC * KC), st,
-                           m_fhi, m_flo, m_l, w.ln2x, c.Nc, c.S, p.K, w.partial, first ? 0 : 1));
-  mark(st, "tc_stats_kernel");
-  return FGMM_OK;
-}
-
-template <int NKC>
-int tc_launch(const TcPlan &p, const float *X, const float *pts, const TcWs &w, float *ln,
-              cudaStream_t st) {
-  std::atomic<bool> &done = device_once_flag(8 + NKC / 2);
-  if (!done) {
-    FGMM_CUDA_TRY(cudaFuncSetAttribute(tc_pass1_kernel<NKC>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1_bytes()));
-    FGMM_CUDA_TRY(cudaFuncSetAttribute(tc_stats_kernel<NKC>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2_bytes(NKC * KC)));
-    done = true;
+  switch (p.nkcf) {
+    case 1: return launch_stats<1>(p, c, pp, n0, w, first, st);
+    case 2: return launch_stats<2>(p, c, pp, n0, w, first, st);
+    case 3: return launch_stats<3>(p, c, pp, n0, w, first, st);
+    case 4: return launch_stats<4>(p, c, pp, n0, w, first, st);
+    default: return fail(FGMM_ERR_UNSUPPORTED, "tcgen05 family: d > 128");
   }
-  for (int i = 0; i < p.chunks; ++i) {
-    const int64_t n0 = (int64_t)i * p.Nc;
-    const int64_t nc = std::min<int64_t>(p.Nc, p.N - n0);
-    const TcChunk c = nc == p.first.Nc ? p.first : chunk_plan(nc, p.n_ct);
-    const int rc = tc_launch_chunk<NKC>(p, c, n0, i == 0, X, pts, w, ln, st);
-    if (rc) return rc;
-  }
-  return FGMM_OK;
 }
 
 }  // namespace
 
 int tc_launches(int64_t N, int d, int K) { return 2 + 3 * plan(N, d, K).chunks; }
 
-bool tc_supported(int64_t N, int d, int K) { return N >= 1 && K >= 1 && d >= 1 && d <= kMaxDp; }
+bool tc_supported(int64_t N, int d, int K) { return N >= 1 && K >= 1 && d >= 1 && d <= kMaxD; }
 
-size_t tc_points_bytes(int64_t N, int d) { return points_half_floats(N, d) * sizeof(float) * 2; }
+size_t tc_points_bytes(int64_t N, int d) {
+  return kPtsHeader + 2 * (p_elems(N, d) + f_elems(N, d)) * sizeof(__half);
+}
 
 size_t tc_workspace_bytes(int64_t N, int d, int K) { return tc_layout(nullptr, plan(N, d, K)).bytes; }
 
 int tc_prepare_points(const float *X, int64_t N, int d, void *points, cudaStream_t st) {
-  const int dp = dp_of(d);
-  float *phi = static_cast<float *>(points);
-  float *plo = phi + points_half_floats(N, d);
-  const int64_t total = npad_of(N) * dp;
-  const int blocks = (int)std::min<int64_t>(cdiv(total, 256), 16 * num_sms());
-  tc_prep_points_kernel<<<blocks, 256, 0, st>>>(X, N, npad_of(N), d, dp, phi, plo);
+  const PtsPtrs pp = pts_ptrs(points, N, d);
+  FGMM_CUDA_TRY(cudaMemsetAsync(points, 0, kPtsHeader, st));
+  const int sms = num_sms();
+  tc_xmax_kernel<<<(unsigned)std::min<int64_t>(N, 8 * sms), 128, 0, st>>>(X, N, d, pp.xmax);
+  FGMM_LAUNCH_CHECK("tc_xmax_kernel");
+  const int kbp = tc_kbp(d), ka = 2 * tc_dp(d);
+  const int64_t total = npad_of(N) * (kbp + ka);
+  const int blocks = (int)std::min<int64_t>(cdiv(total, 256), 16 * sms);
+  tc_prep_points_kernel<<<blocks, 256, 0, st>>>(X, N, npad_of(N), d, kbp, ka, pp.xmax,
+                                                const_cast<int *>(pp.aexp), pp.phi, pp.plo, pp.fhi,
+                                                pp.flo);
   FGMM_LAUNCH_CHECK("tc_prep_points_kernel");
   return FGMM_OK;
 }
@@ -1155,29 +1225,26 @@ int tc_em_stats(const float *X, const void *points, int64_t N, int d, const floa
                 void *ws, cudaStream_t st, const UpdateOut *update, bool prepared) {
   const TcPlan p = plan(N, d, K);
   const TcWs w = tc_layout(ws, p);
+  const PtsPtrs pp = pts_ptrs(points, N, d);
+  const TcParamOps ops = param_ops(w, p, points);
   // `prepared`: the workspace already holds the operands of (mu, var, log_pi), written by
   // the previous call's fused update
   if (!prepared) {
-    FGMM_CUDA_TRY(launch_pdl(tc_prep_params_kernel, p.Kp, 128, 0, st, mu, var, log_pi, K, d, p.dp,
-                             w.qhi, w.qlo, w.cst2, w.sc, w.ms, w.lc));
+    FGMM_CUDA_TRY(launch_pdl(tc_prep_params_kernel, p.Kp, 128, 0, st, mu, var, log_pi, K, d, ops));
     mark(st, "tc_prep_params_kernel");
   }
   UpdateOut up{};
   if (update) {  // the update also prepares the next iteration's operands
     up = *update;
-    up.qhi = w.qhi; up.qlo = w.qlo; up.cst2 = w.cst2; up.sc = w.sc; up.ms = w.ms; up.lc = w.lc;
-    up.dp = p.dp;
+    up.tc = ops;
   }
-  const float *pts = static_cast<const float *>(points);
-  int rc;
-  switch (p.nkc) {
-    case 2: rc = tc_launch<2>(p, X, pts, w, log_norm, st); break;
-    case 4: rc = tc_launch<4>(p, X, pts, w, log_norm, st); break;
-    case 6: rc = tc_launch<6>(p, X, pts, w, log_norm, st); break;
-    case 8: rc = tc_launch<8>(p, X, pts, w, log_norm, st); break;
-    default: return fail(FGMM_ERR_UNSUPPORTED, "tcgen05 family: d > 128");
+  for (int i = 0; i < p.chunks; ++i) {
+    const int64_t n0 = (int64_t)i * p.Nc;
+    const int64_t nc = std::min<int64_t>(p.Nc, p.N - n0);
+    const TcChunk c = nc == p.first.Nc ? p.first : chunk_plan(nc, p.n_ct, p.n_ct2);
+    const int rc = tc_launch_chunk(p, c, n0, i == 0, X, pp, w, log_norm, st);
+    if (rc) return rc;
   }
-  if (rc) return rc;
   return reduce_partials(w.partial, p.first.S, K, d, p.dp, 2 * p.dp + 4, w.ln_part,
                          refine_blocks(p.first.Nc), stats, st, update ? &up : nullptr);
 }

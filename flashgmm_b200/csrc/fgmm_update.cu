@@ -26,8 +26,7 @@ struct UpdateArgs {
   double n_total;
   float *mu, *var, *log_pi;
   int floors, on;
-  float *qhi, *qlo, *cst2, *sc, *ms, *lc;  // next iteration's pass-1 operands (dp > 0)
-  int dp;
+  TcParamOps tc;  // next iteration's tensor-core operands (tc.kbp > 0)
 };
 
 __device__ __forceinline__ float2 update_component(double nk, double s, double q, double n_total,
@@ -118,54 +117,9 @@ reduce_partials_kernel(const float *__restrict__ part, int slots, int K, int d, 
 // multiples of 4, as the tensor-core family writes them): warp w of the block sums slots
 // w, w + 16, ... with float4 loads (lane: four consecutive dimensions), four slots' loads
 // in flight per lane, and the 16 warp sums are added in a fixed order.
-// The pass-1 operands of component k's updated parameters, written by the first 128
-// threads (thread j: dimension j), with tc_prep_params_kernel's arithmetic and its
-// reduction order, so the result is the same as preparing them in the next iteration:
-// Q[k] = [1/var | -2 mu/var] (tf32 hi/lo of the fp64 values), sc = var^-1/2, ms = mu sc,
-// cst2 = log2(e) (log_pi - 1/2 (d log 2pi + sum log var + sum mu^2/var)) and
-// lc = log_pi - 1/2 (d log 2pi + sum log var), from the fp32 values just stored.
-__device__ __forceinline__ float tf32_rn(float x) {
-  uint32_t b = __float_as_uint(x);
-  b = (b + 0x1000u) & 0xFFFFE000u;
-  return __uint_as_float(b);
-}
-__device__ void prep_component(int k, int d, int j, float mu32, float var32, double nk,
-                               const UpdateArgs &up) {
-  __shared__ double red[4], red2[4];
-  const int KA = 2 * up.dp;
-  const int lane = j & 31;
-  double acc = 0.0, acc2 = 0.0;
-  if (j < d) {
-    const double v = var32, m = mu32;
-    const double iv = 1.0 / v, b = -2.0 * m * iv;
-    acc = log(v) + m * m * iv;
-    acc2 = log(v);
-    const double sv = 1.0 / sqrt(v);
-    up.sc[(int64_t)k * d + j] = (float)sv;
-    up.ms[(int64_t)k * d + j] = (float)(m * sv);
-    const float ivh = tf32_rn((float)iv), bh = tf32_rn((float)b);
-    up.qhi[(int64_t)k * KA + j] = ivh;
-    up.qlo[(int64_t)k * KA + j] = tf32_rn((float)(iv - (double)ivh));
-    up.qhi[(int64_t)k * KA + up.dp + j] = bh;
-    up.qlo[(int64_t)k * KA + up.dp + j] = tf32_rn((float)(b - (double)bh));
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    acc2 += __shfl_xor_sync(0xffffffffu, acc2, o);
-  }
-  if (lane == 0) { red[j >> 5] = acc; red2[j >> 5] = acc2; }
-  asm volatile("bar.sync 2, 128;" ::: "memory");  // the first four warps only
-  if (j == 0) {
-    double t1 = 0.0, t2 = 0.0;
-    for (int w = 0; w < 4; ++w) { t1 += red[w]; t2 += red2[w]; }
-    const double lp = (double)(float)(up.floors ? log(fmax(nk / up.n_total, 1e-8))
-                                                : log(nk / up.n_total));
-    up.cst2[k] = (float)(1.4426950408889634 * (lp - 0.5 * (d * kLog2Pi + t1)));
-    up.lc[k] = (float)(lp - 0.5 * (d * kLog2Pi + t2));
-  }
-}
-
+// With the update on, the first 128 threads (thread j: dimension j, d <= 128) also write
+// the next iteration's tensor-core parameter operands of component k's updated values
+// (tc_prep_component, the same arithmetic tc_prep_params_kernel uses).
 constexpr int kRed4Warps = 16;
 __global__ void __launch_bounds__(32 * kRed4Warps)
 reduce_rows4_kernel(const float *__restrict__ part, int slots, int K, int d, int ds, int W,
@@ -233,8 +187,10 @@ reduce_rows4_kernel(const float *__restrict__ part, int slots, int K, int d, int
         mv = update_component(nk, sv, qv, up.n_total, up.floors, up.mu + (int64_t)k * d + jj,
                               up.var + (int64_t)k * d + jj);
     }
-    if (up.on && up.dp > 0 && t < 128)  // d <= 128: one pass; the operands of the new values
-      prep_component(k, d, t, mv.x, mv.y, nk, up);
+    if (up.on && up.tc.kbp > 0 && t < 128) {  // d <= 128: one pass; operands of the new values
+      const float lp32 = (float)(up.floors ? log(fmax(nk / up.n_total, 1e-8)) : log(nk / up.n_total));
+      tc_prep_component(k, K, d, t, mv.x, mv.y, lp32, up.tc, 2);
+    }
     __syncthreads();
   }
   if (t == 0) {
@@ -255,20 +211,14 @@ int reduce_partials(const float *partials, int slots, int K, int d, int ds, int 
     up.log_pi = update->log_pi;
     up.floors = update->floors ? 1 : 0;
     up.on = 1;
-    up.qhi = update->qhi;
-    up.qlo = update->qlo;
-    up.cst2 = update->cst2;
-    up.sc = update->sc;
-    up.ms = update->ms;
-    up.lc = update->lc;
-    up.dp = update->dp;
+    up.tc = update->tc;
   }
 #ifndef FGMM_RED_ROWS4
 #define FGMM_RED_ROWS4 1
 #endif
-  if (up.dp > 0 && !(ds % 4 == 0 && W % 4 == 0 && d <= 128 && reinterpret_cast<uintptr_t>(partials) % 16 == 0))
+  if (up.tc.kbp > 0 && !(ds % 4 == 0 && W % 4 == 0 && d <= 128 && reinterpret_cast<uintptr_t>(partials) % 16 == 0))
     return fail(FGMM_ERR_UNSUPPORTED, "fused parameter preparation needs the aligned row reduction");
-  if (up.dp > 0 || (FGMM_RED_ROWS4 && ds % 4 == 0 && W % 4 == 0 && reinterpret_cast<uintptr_t>(partials) % 16 == 0))
+  if (up.tc.kbp > 0 || (FGMM_RED_ROWS4 && ds % 4 == 0 && W % 4 == 0 && reinterpret_cast<uintptr_t>(partials) % 16 == 0))
     FGMM_CUDA_TRY(launch_pdl(reduce_rows4_kernel, K + 1, 32 * kRed4Warps, 0, stream, partials,
                              slots, K, d, ds, W, ln_partials, ln_slots, stats, up));
   else

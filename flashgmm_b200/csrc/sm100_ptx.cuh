@@ -27,6 +27,7 @@ enum : int {
   kErrWaitGammaEmpty = 6,
   kErrWaitStatsDone = 7,
   kErrWaitDrain = 8,
+  kErrWaitPoints = 9,
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -245,6 +246,27 @@ __device__ __forceinline__ void mma_tf32_ta(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (A and B both fp16), fp32 accumulate.
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16: A (M rows on the TMEM lanes, two fp16
+// K elements per 32-bit column, the lower K index in the low half) from tensor memory.
+__device__ __forceinline__ void mma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on `bar` once all previously issued tcgen05 async ops of this thread complete.
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile(
@@ -307,6 +329,13 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
       : "memory");
 }
 
+// 32 lanes x 4 columns of 32-bit values from registers into TMEM.
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t (&v)[4]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(v[0]),
+               "r"(v[1]), "r"(v[2]), "r"(v[3])
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -367,6 +396,15 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t
 }
 __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   return sdesc(saddr, lbo, sbo, kSw128);
+}
+
+// Instruction descriptor, kind::f16 with fp16 A and B and fp32 accumulate.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int a_mn, int b_mn) {
+  return (1u << 4)                          // D format f32
+         | (0u << 7)                        // A format f16
+         | (0u << 10)                       // B format f16
+         | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 // Instruction descriptor, kind::tf32 with fp32 accumulate.
