@@ -47,6 +47,13 @@ constexpr float kNear = FGMM_NEAR;
 
 inline int64_t npad_of(int64_t N) { return cdiv(N, BM) * BM; }
 
+// Layout shared by pass 1 and the statistics pass: the statistics CTAs own 128 components
+// each and take points in slices of 32; bit p of word
+// xmask[(tile * n_slices + slice) * 128 + c] is set when component c of the tile is one of
+// the exactly evaluated leading components of point p of the slice.
+constexpr int NC2_ref = 128;
+constexpr int kSlice_ref = 32;
+
 // Prepared points: header (column exponents, max |x|), then P hi / lo [Npad][KBp] and
 // F hi / lo [Npad][KA], fp16.  Rows >= N are zero, so no TMA box leaves the tensor.
 inline size_t p_elems(int64_t N, int d) { return align_up((size_t)npad_of(N) * tc_kbp(d), 128); }
@@ -229,7 +236,7 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
                 const float *__restrict__ coef, const float *__restrict__ cst2, int64_t N, int n_pt,
                 int n_ct, int G, int tpg, float *__restrict__ part_m, float *__restrict__ part_s,
                 float4 *__restrict__ part_tv, int4 *__restrict__ part_ti, float *__restrict__ Lt,
-                int64_t Npad) {
+                int64_t Npad, uint32_t *__restrict__ xmask, int64_t xmask_words) {
   using Sh = Pass1Shape<NKC, NC>;
   constexpr int S = Sh::S;
   using Part = typename Sh::Part;
@@ -268,7 +275,10 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
   const int n_units = n_pt * G;
 
   if (warp == 0) {
-    if (lane == 0) {
+    if (lane != 0) {  // the idle lanes clear the exact-component words the refinement sets
+      for (int64_t i = (int64_t)blockIdx.x * 31 + lane - 1; i < xmask_words; i += (int64_t)gridDim.x * 31)
+        xmask[i] = 0u;
+    } else {
       prefetch_tmap(&tm_phi); prefetch_tmap(&tm_plo); prefetch_tmap(&tm_qhi); prefetch_tmap(&tm_qlo);
       // the points stream through once per component group; the parameters are re-read
       const uint64_t pol_p = policy_evict_first(), pol_q = policy_evict_last();
@@ -371,6 +381,10 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
             ++tcount;
           }
           const int k0 = kb + h * 32;
+#ifdef FGMM_EXP_EPI_NOOP
+          m = fmaxf(m, w[h]);
+          continue;
+#endif
           float c4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {
@@ -388,25 +402,32 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
           {  // the log2-likelihood block, transposed: a warp's store is 32 consecutive points
             float *lp = Lt + (int64_t)k0 * Npad + n_row;
 #pragma unroll
-            for (int e = 0; e < 32; ++e) st_hint(lp + (int64_t)e * Npad, w[e], pol_l);
+            for (int e = 0; e < 32; ++e, lp += Npad) st_hint(lp, w[e], pol_l);
           }
 #endif
           // A value enters the leading four only if it lies within kNear of the point's
-          // running maximum (the refinement re-evaluates nothing further below); every
-          // other value, and every value the four push out, joins the rest, whose
-          // reference is its true maximum (so its sum never underflows to zero).
-          const float thr = fmaxf(tv[0], cm) - kNear;
+          // running maximum (the refinement re-evaluates nothing further below).  Only a
+          // half whose maximum comes that close is scanned: its qualifying values are
+          // pushed in turn and w[] then holds the values that drop out.  Every other value
+          // joins the rest, whose reference is its true maximum (so its sum never
+          // underflows to zero).
+          float mn;
+          if (cm > tv[0] - kNear) {
+            const float thr = fmaxf(tv[0], cm) - kNear;
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            if (w[e] > thr && w[e] > tv[3]) {
-              int di;
-              top_push(tv, ti, w[e], k0 + e, w[e], di);  // w[e] becomes the dropped value
+            for (int e = 0; e < 32; ++e) {
+              if (w[e] > thr && w[e] > tv[3]) {
+                int di;
+                top_push(tv, ti, w[e], k0 + e, w[e], di);  // w[e] becomes the dropped value
+              }
             }
-          }
-          float r4[4] = {m, -INFINITY, -INFINITY, -INFINITY};
+            float r4[4] = {m, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-          for (int e = 0; e < 32; ++e) r4[e & 3] = fmaxf(r4[e & 3], w[e]);
-          const float mn = fmaxf(fmaxf(r4[0], r4[1]), fmaxf(r4[2], r4[3]));
+            for (int e = 0; e < 32; ++e) r4[e & 3] = fmaxf(r4[e & 3], w[e]);
+            mn = fmaxf(fmaxf(r4[0], r4[1]), fmaxf(r4[2], r4[3]));
+          } else {
+            mn = fmaxf(m, cm);
+          }
           const float mr = (mn == -INFINITY) ? 0.0f : mn;
           float a4[4] = {s * ex2(m - mr), 0.0f, 0.0f, 0.0f};
 #pragma unroll
@@ -474,7 +495,8 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
                  const float *__restrict__ part_m, const float *__restrict__ part_s,
                  const float4 *__restrict__ part_tv, const int4 *__restrict__ part_ti, int G,
                  float *__restrict__ ln2x, int4 *__restrict__ top_i, float4 *__restrict__ top_d,
-                 float *__restrict__ ln_out, double *__restrict__ ln_part, int acc_ln) {
+                 uint32_t *__restrict__ xmask, int64_t msl, float *__restrict__ ln_out,
+                 double *__restrict__ ln_part, int acc_ln) {
   __shared__ double wsum[8];
   griddep_launch();
   griddep_wait();
@@ -555,20 +577,28 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
       for (int o = 4; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
       if (need) v[c] = (__ldg(lc + kc) - 0.5 * p) * 1.4426950408889634;
     }
-    // the sum in fp64: the rest (fp32 tensor-core values), plus the leading four
+    // the sum: the rest (fp32 tensor-core values), plus the leading four; terms relative to
+    // the maximum in fp32, the maximum itself kept in fp64
     double m = (double)mx;
 #pragma unroll
     for (int c = 0; c < kTcTop; ++c) m = fmax(m, v[c]);
     const double mr = m == -INFINITY ? 0.0 : m;
-    double tot = (double)sm * exp2((double)mx - mr);
+    float tot = sm * exp2f((float)((double)mx - mr));
 #pragma unroll
-    for (int c = 0; c < kTcTop; ++c) tot += exp2(v[c] - mr);
-    const double ln2 = mr + log2(tot);
+    for (int c = 0; c < kTcTop; ++c) tot += exp2f((float)(v[c] - mr));
+    const float lt = log2f(tot);
+    const double ln2 = mr + (double)lt;
     if (live && sub == 0) {
       ln2x[n] = (float)ln2;
       top_i[n] = make_int4(ex[0] ? jx[0] : -1, ex[1] ? jx[1] : -1, ex[2] ? jx[2] : -1, ex[3] ? jx[3] : -1);
-      top_d[n] = make_float4((float)(v[0] - ln2), (float)(v[1] - ln2), (float)(v[2] - ln2),
-                             (float)(v[3] - ln2));
+      top_d[n] = make_float4((float)(v[0] - mr) - lt, (float)(v[1] - mr) - lt, (float)(v[2] - mr) - lt,
+                             (float)(v[3] - mr) - lt);
+      // mark the point in the (component tile, slice) words of its exact components
+#pragma unroll
+      for (int c = 0; c < kTcTop; ++c)
+        if (ex[c])
+          atomicOr(xmask + ((int64_t)(jx[c] / NC2_ref) * msl + n / kSlice_ref) * NC2_ref + jx[c] % NC2_ref,
+                   1u << (n % kSlice_ref));
       const double l = ln2 * 0.6931471805599453;
       ln_out[n] = (float)l;
       acc += l;
@@ -612,7 +642,8 @@ constexpr int kThreads2 = 512;
 constexpr int kGammaWarps = 8;
 constexpr int kGPts = kSlicePts / 2;  // points of a slice per gamma warp
 constexpr int kGCols = kSlicePts;     // TMEM columns of one gamma buffer: hi 16 | lo 16
-constexpr int NC2 = 128;    // components per statistics CTA
+constexpr int NC2 = NC2_ref;  // components per statistics CTA
+static_assert(kSlicePts == kSlice_ref, "one bit per point of a slice");
 
 template <int KA>
 struct StatsShape {
@@ -621,7 +652,8 @@ struct StatsShape {
   static constexpr int kLOff = 2 * kFPart;                     // Lt tile [128][32], 128B-swizzled
   static constexpr int kNOff = kLOff + kSlicePts * NC2 * 4;    // ln2 [32]
   static constexpr int kTOff = kNOff + kSlicePts * 4;          // exact leaders: int4 [32], float4 [32]
-  static constexpr int kStage = (kTOff + kSlicePts * 32 + 1023) / 1024 * 1024;
+  static constexpr int kMOff = kTOff + kSlicePts * 32;         // exact-component bit words [128]
+  static constexpr int kStage = (kMOff + NC2 * 4 + 1023) / 1024 * 1024;
   static constexpr int kStagesFit = (220 * 1024) / kStage;
   static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
   static constexpr int kSmem = 1024 + kStages * kStage + 512;
@@ -631,20 +663,15 @@ __device__ __forceinline__ bool cta_sync_and(bool v) {
   return __syncthreads_and(v ? 1 : 0) != 0;
 }
 
-// Two fp16 K elements in one 32-bit TMEM column: the lower K index in the low half.
-__device__ __forceinline__ uint32_t pack_half2(__half lo_k, __half hi_k) {
-  return (uint32_t)__half_as_ushort(lo_k) | ((uint32_t)__half_as_ushort(hi_k) << 16);
-}
-
 // Partial statistics row (per component and CTA slot, partial[k][slot]):
 // [s (DP) | sq (DP) | n | pad], stride 2 DP + 4, unscaled fp32.
 template <int NKCF>
 __global__ void __launch_bounds__(kThreads2, 1)
 tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constant__ CUtensorMap tm_flo,
                 const __grid_constant__ CUtensorMap tm_l, const float *__restrict__ ln2x,
-                const int4 *__restrict__ top_i, const float4 *__restrict__ top_d, int64_t N,
-                int S_slots, int K, int d, const int *__restrict__ aexp, float *__restrict__ partial,
-                int accum) {
+                const int4 *__restrict__ top_i, const float4 *__restrict__ top_d,
+                const uint32_t *__restrict__ xmask, int64_t msl, int64_t N, int S_slots, int K, int d,
+                const int *__restrict__ aexp, float *__restrict__ partial, int accum) {
   constexpr int KA = NKCF * 64;
   constexpr int DP = KA / 2;
   constexpr int PSTRIDE = 2 * DP + 4;
@@ -742,7 +769,6 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
   if (warp < kGammaWarps) {
     // ---------------- gamma warps
     const int p0 = (warp >> 2) * kGPts;  // this warp's points of each slice
-    const float gscale = (float)(1 << kTcGammaExp);
     for (int s = 0; s < S && ok; ++s) {
       // Tile j is drained once this warp is kGBufs slices into tile j + 1: having waited
       // for the MMAs of slice 8j + 7 it finds tile j complete, and the drain comes before
@@ -763,9 +789,10 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
       const int4 *ti_s = reinterpret_cast<const int4 *>(stg + Sh::kTOff);
       const float4 *td_s = reinterpret_cast<const float4 *>(stg + Sh::kTOff + kSlicePts * 16);
       const int kabs = ct * NC2 + cl;
+      const uint32_t xw = reinterpret_cast<const uint32_t *>(stg + Sh::kMOff)[cl] >> p0;
       const int64_t nb = (s0 + s) * kSlicePts;
       const int live = (N - nb < kSlicePts ? (int)(N - nb) : kSlicePts) - p0;
-      __half gh[kGPts], gl[kGPts];
+      float g[kGPts];
 #pragma unroll
       for (int c = 0; c < kGPts / 4; ++c) {
         const float4 l4 = ln4[p0 / 4 + c];
@@ -775,28 +802,33 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int p = c * 4 + e;
-          // base-2 log-responsibility: the exact value for the point's re-evaluated
-          // leading components, else the tensor-core value
-          const int4 ti = ti_s[p0 + p];
-          const float4 td = td_s[p0 + p];
+          // base-2 log-responsibility (scaled by 2^14): the tensor-core value, or, for the
+          // point's exactly evaluated leading components (marked in xw), the exact one
           float dl = lv[e] - ln2[e];
-          dl = kabs == ti.x ? td.x : dl;
-          dl = kabs == ti.y ? td.y : dl;
-          dl = kabs == ti.z ? td.z : dl;
-          dl = kabs == ti.w ? td.w : dl;
-          const float g = p < live ? ex2(dl) : 0.0f;
-          nk += g;
-          split_f16f(g * gscale, gh[p], gl[p]);
+          if ((xw >> p) & 1u) {
+            const int4 ti = ti_s[p0 + p];
+            const float4 td = td_s[p0 + p];
+            dl = kabs == ti.x ? td.x : (kabs == ti.y ? td.y : (kabs == ti.z ? td.z : td.w));
+          }
+#ifdef FGMM_EXP_NO_GAMMA
+          g[p] = 0.5f;
+#else
+          g[p] = p < live ? ex2(dl + (float)kTcGammaExp) : 0.0f;
+#endif
+          nk += g[p];
         }
+      }
+      uint32_t hi8[kGPts / 2], lo8[kGPts / 2];
+#pragma unroll
+      for (int i = 0; i < kGPts / 2; ++i) {  // fp16 hi / lo pairs, two points per 32-bit column
+        const __half2 h = __floats2half2_rn(g[2 * i], g[2 * i + 1]);
+        const float2 hf = __half22float2(h);
+        const __half2 l = __floats2half2_rn(g[2 * i] - hf.x, g[2 * i + 1] - hf.y);
+        hi8[i] = *reinterpret_cast<const uint32_t *>(&h);
+        lo8[i] = *reinterpret_cast<const uint32_t *>(&l);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(EMPTY(st));  // this warp is done with the slice's Lt
-      uint32_t hi8[kGPts / 2], lo8[kGPts / 2];
-#pragma unroll
-      for (int i = 0; i < kGPts / 2; ++i) {
-        hi8[i] = pack_half2(gh[2 * i], gh[2 * i + 1]);
-        lo8[i] = pack_half2(gl[2 * i], gl[2 * i + 1]);
-      }
       const uint32_t ga = lane_tmem + kGBase + gb * kGCols + p0 / 2;
       tmem_st8(ga, *reinterpret_cast<const float(*)[8]>(hi8));
       tmem_st8(ga + kSlicePts / 2, *reinterpret_cast<const float(*)[8]>(lo8));
@@ -828,6 +860,7 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
         const uint64_t fd = fdesc0 + (uint64_t)((st * Sh::kStage) >> 4);
         constexpr uint64_t kLo = Sh::kFPart >> 4, kK = (16 * 128) >> 4;  // k-step: 16 points
         constexpr uint32_t kGLo = kSlicePts / 2;                          // gamma lo columns
+#ifndef FGMM_EXP_NO_MMA2
 #pragma unroll
         for (int kk = 0; kk < kSlicePts / 16; ++kk) {
           mma_f16_ta(dst, gbuf + kGLo + kk * 8, fd + kk * kK, idesc, (tile_first && kk == 0) ? 0u : 1u);
@@ -835,6 +868,7 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
         }
 #pragma unroll
         for (int kk = 0; kk < kSlicePts / 16; ++kk) mma_f16_ta(dst, gbuf + kk * 8, fd + kk * kK, idesc, 1u);
+#endif
         mma_commit(EMPTY(st));
         mma_commit(GEMPTY(gb));
         if (s % kSlicesFlush == kSlicesFlush - 1 || s == S - 1) mma_commit(SFULL(reg));
@@ -865,13 +899,15 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
       if (lane == 0) {
         const uint32_t base = smem_u32(smem + st * Sh::kStage);
         const int64_t nb = (s0 + s) * kSlicePts;
-        mbar_arrive_expect_tx(FULL(st), 2 * Sh::kFPart + kSlicePts * NC2 * 4 + kSlicePts * 36);  // F, Lt, ln2, leaders
+        // F, Lt, ln2, leaders, exact-component words
+        mbar_arrive_expect_tx(FULL(st), 2 * Sh::kFPart + kSlicePts * NC2 * 4 + kSlicePts * 36 + NC2 * 4);
         tma_load_3d(base, &tm_fhi, 0, (int32_t)nb, 0, FULL(st));
         tma_load_3d(base + Sh::kFPart, &tm_flo, 0, (int32_t)nb, 0, FULL(st));
         tma_load_2d_hint(base + Sh::kLOff, &tm_l, (int32_t)nb, ct * NC2, FULL(st), pol_l);
         bulk_load(base + Sh::kNOff, ln2x + nb, kSlicePts * 4, FULL(st));
         bulk_load(base + Sh::kTOff, top_i + nb, kSlicePts * 16, FULL(st));
         bulk_load(base + Sh::kTOff + kSlicePts * 16, top_d + nb, kSlicePts * 16, FULL(st));
+        bulk_load(base + Sh::kMOff, xmask + ((int64_t)ct * msl + s0 + s) * NC2, NC2 * 4, FULL(st));
       }
       __syncwarp();
     }
@@ -912,7 +948,7 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
   __syncthreads();
   if (warp < 4 && k < K) {
     float *o = partial + ((int64_t)k * S_slots + slot) * PSTRIDE + 2 * DP;
-    const float v = ok ? nk + nk_s[cl] : 0.0f;
+    const float v = ok ? ldexpf(nk + nk_s[cl], -kTcGammaExp) : 0.0f;
     *o = accum ? *o + v : v;
   }
   tc_fence_before();
@@ -1035,6 +1071,8 @@ struct TcWs {
   double *lc;
   float4 *part_tv, *top_d;
   int4 *part_ti, *top_i;
+  uint32_t *xmask;
+  int64_t msl;  // slices of 32 points per chunk (the bit words' stride)
   double *ln_part;
   size_t bytes;
 };
@@ -1062,6 +1100,8 @@ TcWs tc_layout(void *ws, const TcPlan &p) {
   w.ln2x = c.take<float>(npad_of(Nc));
   w.top_i = c.take<int4>(npad_of(Nc));
   w.top_d = c.take<float4>(npad_of(Nc));
+  w.msl = npad_of(Nc) / kSlice_ref;
+  w.xmask = c.take<uint32_t>((size_t)p.n_ct2 * w.msl * NC2_ref);
   w.partial = c.take<float>((size_t)p.first.S * p.K * (2 * p.dp + 4));
   w.ln_part = c.take<double>(kRefineBlocks);
   w.L = c.take<float>((size_t)npad_of(Nc) * p.Kp);  // Lt [Kp][chunk]
@@ -1109,7 +1149,8 @@ int launch_pass1(const TcPlan &p, const TcChunk &c, const PtsPtrs &pp, int64_t n
   if ((rc = make_map(&m_qlo, w.qlo, F16, 2, p.Kp, p.kbp, NC, KCH, SW))) return rc;
   FGMM_CUDA_TRY(launch_pdl(tc_pass1_kernel<NKC, NC>, c.grid1, kThreads1, Sh::kSmem, st, m_phi, m_plo,
                            m_qhi, m_qlo, w.coef, w.cst2, c.Nc, c.n_pt, p.n_ct, c.G, c.tpg, w.part_m,
-                           w.part_s, w.part_tv, w.part_ti, w.L, rows));
+                           w.part_s, w.part_tv, w.part_ti, w.L, rows, w.xmask,
+                           (int64_t)p.n_ct2 * w.msl * NC2_ref));
   mark(st, "tc_pass1_kernel");
   return FGMM_OK;
 }
@@ -1135,7 +1176,8 @@ int launch_stats(const TcPlan &p, const TcChunk &c, const PtsPtrs &pp, int64_t n
                      CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
   FGMM_CUDA_TRY(launch_pdl(tc_stats_kernel<NKCF>, c.grid2, kThreads2, StatsShape<KA>::kSmem, st,
-                           m_fhi, m_flo, m_l, w.ln2x, w.top_i, w.top_d, c.Nc, c.S, p.K, p.d, pp.aexp,
+                           m_fhi, m_flo, m_l, w.ln2x, w.top_i, w.top_d, w.xmask, w.msl, c.Nc, c.S,
+                           p.K, p.d, pp.aexp,
                            w.partial,
                            first ? 0 : 1));
   mark(st, "tc_stats_kernel");
@@ -1167,11 +1209,11 @@ int tc_launch_chunk(const TcPlan &p, const TcChunk &c, int64_t n0, bool first, c
     if (vec && (D) % 4 == 0 && 8 * (D) == p.d)                                                     \
       FGMM_CUDA_TRY(launch_pdl(tc_refine_kernel<D, true>, blocks, 256, 0, st, Xc, c.Nc, p.d, w.sc, \
                                w.mu, w.lc, w.part_m, w.part_s, w.part_tv, w.part_ti, c.G, w.ln2x,  \
-                               w.top_i, w.top_d, ln + n0, w.ln_part, acc));                        \
+                               w.top_i, w.top_d, w.xmask, w.msl, ln + n0, w.ln_part, acc));        \
     else                                                                                           \
       FGMM_CUDA_TRY(launch_pdl(tc_refine_kernel<D, false>, blocks, 256, 0, st, Xc, c.Nc, p.d, w.sc,\
                                w.mu, w.lc, w.part_m, w.part_s, w.part_tv, w.part_ti, c.G, w.ln2x,  \
-                               w.top_i, w.top_d, ln + n0, w.ln_part, acc));                        \
+                               w.top_i, w.top_d, w.xmask, w.msl, ln + n0, w.ln_part, acc));        \
   } while (0)
     if (dpl <= 1) FGMM_REFINE(1);
     else if (dpl <= 2) FGMM_REFINE(2);

@@ -177,9 +177,10 @@ __device__ __forceinline__ void tma_load_3d_hint(uint32_t dst, const CUtensorMap
       : "memory");
 }
 
-// fp32 store with an L2 eviction policy.
+// fp32 store with an L2 eviction policy.  No memory clobber: the stored data is read only
+// by later kernels, so the compiler may move loads and stores of this kernel around it.
 __device__ __forceinline__ void st_hint(float *p, float v, uint64_t policy) {
-  asm volatile("st.global.L2::cache_hint.f32 [%0], %1, %2;" ::"l"(p), "f"(v), "l"(policy) : "memory");
+  asm volatile("st.global.L2::cache_hint.f32 [%0], %1, %2;" ::"l"(p), "f"(v), "l"(policy));
 }
 
 // 3-D tile load (same completion mechanism as tma_load_2d).
