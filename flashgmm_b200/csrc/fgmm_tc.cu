@@ -40,10 +40,7 @@ constexpr float kLn2 = 0.6931471805599453f;
 constexpr int kMaxD = 128;                     // d <= 128 runs here
 // Leading components more than kNear below a point's largest base-2 log-likelihood have
 // responsibilities below 2^-kNear relative to the leader and are not re-evaluated.
-#ifndef FGMM_NEAR
-#define FGMM_NEAR 32.0f
-#endif
-constexpr float kNear = FGMM_NEAR;
+constexpr float kNear = 32.0f;
 
 inline int64_t npad_of(int64_t N) { return cdiv(N, BM) * BM; }
 
@@ -381,10 +378,6 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
             ++tcount;
           }
           const int k0 = kb + h * 32;
-#ifdef FGMM_EXP_EPI_NOOP
-          m = fmaxf(m, w[h]);
-          continue;
-#endif
           float c4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {
@@ -398,13 +391,11 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
             for (int r = 0; r < 4; ++r) c4[r] = fmaxf(c4[r], w[e + r]);
           }
           const float cm = fmaxf(fmaxf(c4[0], c4[1]), fmaxf(c4[2], c4[3]));
-#ifndef FGMM_EXP_NO_LT
           {  // the log2-likelihood block, transposed: a warp's store is 32 consecutive points
             float *lp = Lt + (int64_t)k0 * Npad + n_row;
 #pragma unroll
             for (int e = 0; e < 32; ++e, lp += Npad) st_hint(lp, w[e], pol_l);
           }
-#endif
           // A value enters the leading four only if it lies within kNear of the point's
           // running maximum (the refinement re-evaluates nothing further below).  Only a
           // half whose maximum comes that close is scanned: its qualifying values are
@@ -472,6 +463,53 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
   }
 }
 
+// Exact squared distances of one point (eight lanes, dimension i * 8 + sub per lane) to
+// two components (index -1: none): sum_j ((x_j - mu_j) var_j^-1/2)^2, each term from the
+// fp32 inputs in fp64 (fp32 terms leave ~10x the error in the variances), reduced over the
+// point's eight lanes.
+template <int DPL, bool VEC>
+__device__ __forceinline__ void exact_pair(const float (&x)[DPL], int sub, int d,
+                                           const float *__restrict__ sc, const float *__restrict__ mu,
+                                           int k0, int k1, double (&p)[2]) {
+  const int kk[2] = {k0, k1};
+  float m[2][DPL], sv[2][DPL];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const bool need = kk[u] >= 0;
+    const int64_t base = (int64_t)(need ? kk[u] : 0) * d;
+    if (VEC) {
+#pragma unroll
+      for (int i = 0; i < DPL / 4; ++i) {
+        const int64_t q = base + (int64_t)(i * 8 + sub) * 4;
+        const float4 m4 = need ? __ldg(reinterpret_cast<const float4 *>(mu + q)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 s4 = need ? __ldg(reinterpret_cast<const float4 *>(sc + q)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        m[u][4 * i] = m4.x; m[u][4 * i + 1] = m4.y; m[u][4 * i + 2] = m4.z; m[u][4 * i + 3] = m4.w;
+        sv[u][4 * i] = s4.x; sv[u][4 * i + 1] = s4.y; sv[u][4 * i + 2] = s4.z; sv[u][4 * i + 3] = s4.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) {
+        const int j = i * 8 + sub;
+        const bool in = need && j < d;
+        m[u][i] = in ? __ldg(mu + base + j) : 0.0f;
+        sv[u][i] = in ? __ldg(sc + base + j) : 0.0f;
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    double a0 = 0.0, a1 = 0.0;  // two chains
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+      const double t = ((double)x[i] - (double)m[u][i]) * (double)sv[u][i];
+      if (i & 1) a1 = fma(t, t, a1); else a0 = fma(t, t, a0);
+    }
+    p[u] = a0 + a1;
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) p[u] += __shfl_xor_sync(0xffffffffu, p[u], o);
+  }
+}
+
 // ------------------------------------------------------------------------- refine
 // Exact re-evaluation of each point's leading components.  The tensor-core
 // log-likelihoods carry an absolute error of ~1e-4 (the products are fp16 hi/lo pairs
@@ -489,7 +527,7 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
 // Eight lanes per point (four points per warp), lanes striped over the dimensions; the
 // point's row is loaded first so its latency overlaps the partial loads.
 template <int DPL, bool VEC>  // dimensions per lane: ceil(d / 8); VEC: vector loads
-__global__ void __launch_bounds__(256, 4)
+__global__ void __launch_bounds__(256, DPL >= 12 ? 2 : 4)
 tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__restrict__ sc,
                  const float *__restrict__ mu, const double *__restrict__ lc,
                  const float *__restrict__ part_m, const float *__restrict__ part_s,
@@ -543,39 +581,18 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
     bool ex[kTcTop];
 #pragma unroll
     for (int c = 0; c < kTcTop; ++c) {
-      const bool need = jx[c] >= 0 && b[c] >= b[0] - kNear;
-      ex[c] = need;
+      ex[c] = jx[c] >= 0 && b[c] >= b[0] - kNear;
       v[c] = jx[c] >= 0 ? (double)b[c] : -INFINITY;
-      if (!__any_sync(0xffffffffu, need)) continue;
-      const int64_t kc = need ? jx[c] : 0;
-      double p = 0.0;
-      if (VEC) {
+    }
+    // two components at a time, all their loads issued before the arithmetic
 #pragma unroll
-        for (int i = 0; i < DPL / 4; ++i) {
-          const int64_t q = kc * d + (int64_t)(i * 8 + sub) * 4;
-          const float4 m4 = need ? __ldg(reinterpret_cast<const float4 *>(mu + q)) : make_float4(0.f, 0.f, 0.f, 0.f);
-          const float4 s4 = need ? __ldg(reinterpret_cast<const float4 *>(sc + q)) : make_float4(0.f, 0.f, 0.f, 0.f);
-          // fp64 difference and scale (fp32 here leaves ~10x the error in the variances)
-          const double t0 = ((double)x[4 * i] - m4.x) * (double)s4.x;
-          const double t1 = ((double)x[4 * i + 1] - m4.y) * (double)s4.y;
-          const double t2 = ((double)x[4 * i + 2] - m4.z) * (double)s4.z;
-          const double t3 = ((double)x[4 * i + 3] - m4.w) * (double)s4.w;
-          p = fma(t0, t0, p); p = fma(t1, t1, p); p = fma(t2, t2, p); p = fma(t3, t3, p);
-        }
-      } else {
+    for (int c = 0; c < kTcTop; c += 2) {
+      if (!__any_sync(0xffffffffu, ex[c] || ex[c + 1])) continue;
+      double p[2];
+      exact_pair<DPL, VEC>(x, sub, d, sc, mu, ex[c] ? jx[c] : -1, ex[c + 1] ? jx[c + 1] : -1, p);
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) {
-          const int j = i * 8 + sub;
-          const bool in = need && j < d;
-          const float s1 = in ? __ldg(sc + kc * d + j) : 0.0f;
-          const float m1 = in ? __ldg(mu + kc * d + j) : 0.0f;
-          const double t = ((double)x[i] - m1) * (double)s1;
-          p = fma(t, t, p);
-        }
-      }
-#pragma unroll
-      for (int o = 4; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
-      if (need) v[c] = (__ldg(lc + kc) - 0.5 * p) * 1.4426950408889634;
+      for (int u = 0; u < 2; ++u)
+        if (ex[c + u]) v[c + u] = (__ldg(lc + jx[c + u]) - 0.5 * p[u]) * 1.4426950408889634;
     }
     // the sum: the rest (fp32 tensor-core values), plus the leading four; terms relative to
     // the maximum in fp32, the maximum itself kept in fp64
@@ -810,11 +827,7 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
             const float4 td = td_s[p0 + p];
             dl = kabs == ti.x ? td.x : (kabs == ti.y ? td.y : (kabs == ti.z ? td.z : td.w));
           }
-#ifdef FGMM_EXP_NO_GAMMA
-          g[p] = 0.5f;
-#else
           g[p] = p < live ? ex2(dl + (float)kTcGammaExp) : 0.0f;
-#endif
           nk += g[p];
         }
       }
@@ -860,7 +873,6 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
         const uint64_t fd = fdesc0 + (uint64_t)((st * Sh::kStage) >> 4);
         constexpr uint64_t kLo = Sh::kFPart >> 4, kK = (16 * 128) >> 4;  // k-step: 16 points
         constexpr uint32_t kGLo = kSlicePts / 2;                          // gamma lo columns
-#ifndef FGMM_EXP_NO_MMA2
 #pragma unroll
         for (int kk = 0; kk < kSlicePts / 16; ++kk) {
           mma_f16_ta(dst, gbuf + kGLo + kk * 8, fd + kk * kK, idesc, (tile_first && kk == 0) ? 0u : 1u);
@@ -868,7 +880,6 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
         }
 #pragma unroll
         for (int kk = 0; kk < kSlicePts / 16; ++kk) mma_f16_ta(dst, gbuf + kk * 8, fd + kk * kK, idesc, 1u);
-#endif
         mma_commit(EMPTY(st));
         mma_commit(GEMPTY(gb));
         if (s % kSlicesFlush == kSlicesFlush - 1 || s == S - 1) mma_commit(SFULL(reg));
@@ -1050,11 +1061,7 @@ TcPlan plan(int64_t N, int d, int K) {
   p.kbp = tc_kbp(d);
   p.nkc = p.kbp / KCH;
   p.nkcf = p.KA / KCH;
-#ifdef FGMM_PASS1_NC128
-  p.NC = 128;
-#else
   p.NC = K <= 128 ? 128 : 256;
-#endif
   p.n_ct = (int)cdiv(K, p.NC);
   p.Kp = p.n_ct * p.NC;
   p.n_ct2 = (int)cdiv(K, NC2);
@@ -1077,7 +1084,7 @@ struct TcWs {
   size_t bytes;
 };
 
-constexpr int kRefineBlocks = 8192;  // 32 points per block
+constexpr int kRefineBlocks = 8192;  // 32 points per block per sweep
 inline int refine_blocks(int64_t N) { return (int)std::min<int64_t>(kRefineBlocks, cdiv(N, 32)); }
 
 // Per-chunk buffers are sized for the first (largest) chunk; the component-group
