@@ -57,16 +57,18 @@ def peaks():
 
 
 def algorithmic(wl, n_points):
-    """Per-iteration algorithmic work of the tensor-core path.
+    """Per-iteration algorithmic work of one EM iteration (the survey's measurement row).
 
-    FLOPs: the two contractions, each 2 N K (2 d) multiply-adds counted as fp32 products
-    (distance GEMM [x^2 | x] . [1/var | -2 mu/var], statistics GEMM gamma^T [x^2 | x]):
-    8 N K d.  Bytes: X read by pass 1, the refine and the statistics pass (3 N d), the
-    log2-likelihood matrix L written once and read once (2 N K), per-point scalars and
-    the parameters (4 N + 4 K d + 2 K), all fp32."""
+    FLOPs, in fp32-product units: each of the two contractions the design executes is
+    2 N K (2 d) multiply-adds = 4 N K d (distance GEMM [x^2 | x] . [1/var | -2 mu/var],
+    statistics GEMM gamma^T [x^2 | x]); 8 N K d per iteration (the reference's recompute
+    design counts a third, 12 N K d, reported beside it).  Bytes: X read once, the
+    log-normalizer written, the parameters read and written and the statistics written:
+    4 (N d + N + 4 K d + 2 K), all fp32.  Whatever the design moves beyond that shows in
+    the measured traffic, not here."""
     N, K, d = n_points, wl.K, wl.d
     flops = 8.0 * N * K * d
-    nbytes = 4.0 * (3 * N * d + 2 * N * K + 4 * N + 4 * K * d + 2 * K)
+    nbytes = 4.0 * (N * d + N + 4 * K * d + 2 * K)
     return flops, nbytes
 
 
@@ -307,9 +309,15 @@ def run_ours(args, wl):
                       prepared=prepared[0])
             prepared[0] = tc_family
             return
-        stats, _ = C.em_stats(X, mu, var, lp, points=points, workspace=ws)
+        # statistics over this rank's shard (the parameter operands left by the previous
+        # update), one all-reduce, the update that also prepares the next operands
+        stats, _ = C.em_stats(X, mu, var, lp, points=points, workspace=ws, prepared=prepared[0])
         dist.all_reduce(stats)
-        mu, var, lp = C.em_update(stats, n_total, K, d)
+        if tc_family:
+            C.em_update_prepared(stats, n_total, points, ws, out=(mu, var, lp))
+            prepared[0] = True
+        else:
+            mu, var, lp = C.em_update(stats, n_total, K, d)
 
     clocks = ClockSampler(gpu_id(dev)).start() if rank == 0 else None
     for _ in range(args.warmup):
@@ -342,32 +350,46 @@ def run_ours(args, wl):
     prof = profile_dominant(C, X, points, mu, var, lp, ws)
     dom = max(prof, key=prof.get)
     pk = peaks()
-    tf32_eff = pk["bf16_tflops"] / 2.0 / 3.0  # 3xTF32: three TF32 products per fp32 product
+    f16x3 = pk["bf16_tflops"] / 3.0  # three fp16 products (kind::f16, bf16 rate) per fp32 product
     flops, nbytes = algorithmic(wl, N)
     gemm = dom in ("tc_pass1_kernel", "tc_stats_kernel")
     if gemm:  # each of the two kernels carries one of the two contractions
         achieved = flops / 2.0 / (prof[dom] * 1e-3) / 1e12
-        roofline = {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": tf32_eff,
-                    "unit": "TFLOP/s", "frac": achieved / tf32_eff}
+        roofline = {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": f16x3,
+                    "unit": "TFLOP/s", "frac": achieved / f16x3}
     else:
         achieved = nbytes / (prof[dom] * 1e-3) / 1e9
         roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": pk["hbm_gbs"],
                     "unit": "GB/s", "frac": achieved / pk["hbm_gbs"]}
     roofline.update({
         "traffic": ncu_traffic(dom, wl.name), "kernel_ms": prof[dom], "launch_ms": prof,
-        "peak_note": (f"3xTF32 effective = {pk['source']} bf16 {pk['bf16_tflops']:.0f} TF/s / 2 "
-                      f"(tf32) / 3 (products); hbm {pk['source']} {pk['hbm_gbs']:.0f} GB/s"),
-        "iteration_frac": (flops / (ms_per_step * 1e-3) / 1e12) / tf32_eff,
+        "peak_note": (f"3xF16 effective = {pk['source']} bf16 {pk['bf16_tflops']:.0f} TF/s / 3 "
+                      f"(three fp16 products per fp32 product); hbm {pk['source']} "
+                      f"{pk['hbm_gbs']:.0f} GB/s"),
+        "iteration_frac": (flops / (ms_per_step * 1e-3) / 1e12) / f16x3,
+        "iteration_frac_12nkd": (1.5 * flops / (ms_per_step * 1e-3) / 1e12) / f16x3,
+        "traffic_over_algorithmic": None,  # set below
         "algorithmic": {"flops_per_iter": flops, "bytes_per_iter": nbytes,
                         "dominant_flops_per_launch": flops / 2.0 if gemm else None}})
 
-    # one EM step: em_stats' launches, less the parameter preparation on one GPU (done by
-    # the previous step's fused update), plus the separate update after the all-reduce
-    launches = lib.fgmm_em_stats_launches(N, d, K) + (1 if ws_n > 1 else (-1 if tc_family else 0))
+    if roofline["traffic"]:
+        roofline["traffic_over_algorithmic"] = roofline["traffic"] / nbytes
+
+    # one EM step: em_stats' launches; on the tensor-core family less the parameter
+    # preparation (the previous update wrote the operands), and on several GPUs plus the
+    # separate update launch after the all-reduce
+    launches = lib.fgmm_em_stats_launches(N, d, K) - (1 if tc_family else 0) + (1 if ws_n > 1 else 0)
     e2e = None
     cpu = None
     if not args.no_e2e:
         e2e = run_e2e(wl, dev, args, ws_n, rank)
+    c5 = None
+    if not args.no_strong_c5:
+        t_n, t_1 = strong_c5(dev, ws_n, rank)
+        if rank == 0:
+            c5 = {"workload": "c5 (N=2^24, K=1024, d=128, points split over the GPUs)",
+                  "ms_per_iter": t_n, "ms_per_iter_1gpu": t_1, "speedup": t_1 / t_n,
+                  "iters": 10, "n_gpus": ws_n}
     if rank == 0 and ws_n == 1 and not args.no_cpu_baseline:
         s_full, sample, kind, threads = cpu_time_per_iter(wl)
         cpu = {"value": 1.0 / s_full, "unit": "iter/s", "cores": threads, "kind": kind,
@@ -383,11 +405,73 @@ def run_ours(args, wl):
                        "family": {1: "simt", 2: "tcgen05", 3: "lowk"}.get(C.family_for(N, d, K), "?"),
                        "l2": "flushed between timed iterations (256 MB write, untimed)"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
-            "gpu_launches": launches * args.steps,
+            "gpu_launches": launches * args.steps, "strong_c5": c5,
         }
         print(json.dumps(line), flush=True)
     if ws_n > 1:
         dist.destroy_process_group()
+
+
+def strong_c5(dev, ws_n, rank, iters=10, warmup=2):
+    """Strong scaling on configuration 5 (N = 2^24 unit-norm points, K = 1024, d = 128): the
+    points are split evenly over the ranks and every iteration all-reduces the statistics.
+    Returns (ms per iteration, max over ranks; ms per iteration of the whole set on rank 0's
+    GPU alone, measured in the same run).  The points are generated on the GPUs (the same
+    distribution as the workload generator: noisy unit directions, renormalised)."""
+    from flashgmm_b200 import flash_gmm_native as C
+    Ntot, K, d = 1 << 24, 1024, 128
+    g = torch.Generator().manual_seed(5)
+    u = torch.randn(K, d, generator=g)
+    u = u / u.norm(dim=1, keepdim=True)
+    mu0 = (u + 0.05 * torch.randn(K, d, generator=g))
+    mu0 = (mu0 / mu0.norm(dim=1, keepdim=True)).to(dev)
+    var0 = torch.ones(K, d, device=dev)
+    lp0 = torch.full((K,), -math.log(K), device=dev)
+    ud = u.to(dev)
+
+    def shard(n, seed):
+        gg = torch.Generator(device=dev).manual_seed(seed)
+        z = torch.randint(0, K, (n,), generator=gg, device=dev)
+        x = ud[z] + 0.05 * torch.randn(n, d, generator=gg, device=dev)
+        return (x / x.norm(dim=1, keepdim=True)).contiguous()
+
+    def run(X, n_total, group_size):
+        pts = C.prepare_points(X, K)
+        ws = C.StatsWorkspace(X.shape[0], d, K, dev)
+        mu, var, lp = mu0.clone(), var0.clone(), lp0.clone()
+        prepared = False
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for it in range(warmup + iters):
+            if it == warmup:
+                torch.cuda.synchronize(dev)
+                if group_size > 1:
+                    dist.barrier()
+                e0.record()
+            stats, _ = C.em_stats(X, mu, var, lp, points=pts, workspace=ws, prepared=prepared)
+            if group_size > 1:
+                dist.all_reduce(stats)
+            C.em_update_prepared(stats, n_total, pts, ws, out=(mu, var, lp))
+            prepared = True
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / iters
+
+    one = None
+    if rank == 0:  # the whole set on one GPU, for the speed-up
+        X = shard(Ntot, 1234)
+        one = run(X, Ntot, 1)
+        del X
+        torch.cuda.empty_cache()
+    if ws_n > 1:
+        dist.barrier()
+        X = shard(Ntot // ws_n, 1000 + rank)
+        t = torch.tensor([run(X, Ntot, ws_n)], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        many = t.item()
+        del X
+    else:
+        many = one
+    return many, one
 
 
 def run_e2e(wl, dev, args, ws_n=1, rank=0, steps=200):
@@ -486,6 +570,7 @@ def main():
     ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS))
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-strong-c5", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

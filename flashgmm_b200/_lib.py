@@ -32,6 +32,8 @@ SIGNATURES = {
     "fgmm_em_stats_workspace_bytes": (_sz, [_i64, _i32, _i32]),
     "fgmm_em_stats": (ctypes.c_int, [_vp, _vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _sz, _vp]),
     "fgmm_em_update": (ctypes.c_int, [_vp, _d, _i32, _i32, _vp, _vp, _vp, _vp]),
+    "fgmm_em_stats_ex": (ctypes.c_int, [_vp, _vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _sz, _i32, _vp]),
+    "fgmm_em_update_prepared": (ctypes.c_int, [_vp, _d, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _sz, _vp]),
     "fgmm_em_update_ex": (ctypes.c_int, [_vp, _d, _i32, _i32, _i32, _vp, _vp, _vp, _vp]),
     "fgmm_em_step": (ctypes.c_int, [_vp, _vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp,
                                     _vp, _sz, _i32, _vp]),

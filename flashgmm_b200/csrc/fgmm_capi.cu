@@ -166,6 +166,33 @@ int fgmm_em_stats(const float *X, const void *points, int64_t N, int32_t d, cons
                        workspace_bytes, stream, nullptr);
 }
 
+int fgmm_em_stats_ex(const float *X, const void *points, int64_t N, int32_t d, const float *mu,
+                     const float *var, const float *log_pi, int32_t K, double *stats,
+                     float *log_normalizer, void *workspace, size_t workspace_bytes, int32_t flags,
+                     void *stream) {
+  if (flags & ~FGMM_STEP_PREPARED) return fail(FGMM_ERR_INVALID, "unknown flags");
+  const bool prepared = (flags & FGMM_STEP_PREPARED) != 0;
+  if (prepared && (!points || resolve_family(N, d, K) != FGMM_FAMILY_TC))
+    return fail(FGMM_ERR_INVALID, "FGMM_STEP_PREPARED needs the tensor-core family and prepared points");
+  return em_stats_impl(X, points, N, d, mu, var, log_pi, K, stats, log_normalizer, workspace,
+                       workspace_bytes, stream, nullptr, prepared);
+}
+
+int fgmm_em_update_prepared(const double *stats, double n_total, const void *points, int64_t N,
+                            int32_t d, int32_t K, float *new_mu, float *new_var, float *new_log_pi,
+                            void *workspace, size_t workspace_bytes, void *stream) {
+  int rc = check_shape(N, d, K);
+  if (rc) return rc;
+  if (!stats || !points || !new_mu || !new_var || !new_log_pi || !workspace)
+    return fail(FGMM_ERR_INVALID, "null pointer argument");
+  if (!(n_total > 0)) return fail(FGMM_ERR_INVALID, "n_total must be > 0");
+  if (resolve_family(N, d, K) != FGMM_FAMILY_TC)
+    return fail(FGMM_ERR_INVALID, "fgmm_em_update_prepared needs the tensor-core family");
+  if (workspace_bytes < tc_workspace_bytes(N, d, K)) return fail(FGMM_ERR_WORKSPACE, "workspace too small");
+  return tc_update_prepare(stats, n_total, points, N, d, K, new_mu, new_var, new_log_pi, workspace,
+                           (cudaStream_t)stream);
+}
+
 int fgmm_em_step(const float *X, const void *points, int64_t N, int32_t d, const float *mu,
                  const float *var, const float *log_pi, int32_t K, float *new_mu, float *new_var,
                  float *new_log_pi, double *stats, float *log_normalizer, void *workspace,

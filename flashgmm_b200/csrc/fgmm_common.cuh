@@ -142,6 +142,14 @@ int tc_em_stats(const float *X, const void *points, int64_t N, int d, const floa
 int reduce_partials(const float *partials, int slots, int K, int d, int ds, int W,
                     const double *ln_partials, int ln_slots, double *stats,
                     cudaStream_t stream, const UpdateOut *update = nullptr);
+// M-step (floored) that also writes the tensor-core operands of the new values.
+int em_update_prep(const double *stats, double n_total, int K, int Kp, int d, float *new_mu,
+                   float *new_var, float *new_log_pi, const TcParamOps &op, cudaStream_t stream);
+// The sharded fit's update step: em_update_prep into the statistics workspace of
+// tc_em_stats for (N, d, K) and these prepared points.
+int tc_update_prepare(const double *stats, double n_total, const void *points, int64_t N, int d,
+                      int K, float *new_mu, float *new_var, float *new_log_pi, void *ws,
+                      cudaStream_t stream);
 int em_update(const double *stats, double n_total, int K, int d, float *new_mu,
               float *new_var, float *new_log_pi, cudaStream_t stream, bool floors = true);
 

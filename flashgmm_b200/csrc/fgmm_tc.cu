@@ -1298,6 +1298,15 @@ int tc_em_stats(const float *X, const void *points, int64_t N, int d, const floa
                          refine_blocks(p.first.Nc), stats, st, update ? &up : nullptr);
 }
 
+int tc_update_prepare(const double *stats, double n_total, const void *points, int64_t N, int d,
+                      int K, float *new_mu, float *new_var, float *new_log_pi, void *ws,
+                      cudaStream_t st) {
+  const TcPlan p = plan(N, d, K);
+  const TcWs w = tc_layout(ws, p);
+  return em_update_prep(stats, n_total, K, p.Kp, d, new_mu, new_var, new_log_pi,
+                        param_ops(w, p, points), st);
+}
+
 int tc_device_error(bool reset) {
   int v = 0;
   if (cudaDeviceSynchronize() != cudaSuccess) return -1;

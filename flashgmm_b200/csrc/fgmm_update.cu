@@ -248,6 +248,38 @@ __global__ void em_update_kernel(const double *__restrict__ stats, double n_tota
     new_log_pi[k] = (float)(floors ? log(fmax(nk / n_total, 1e-8)) : log(nk / n_total));
 }
 
+// em_update_kernel's M-step for d <= 128 (thread j: dimension j, 128 threads), which also
+// writes the next iteration's tensor-core operands of the new values (tc_prep_component):
+// the update step of a sharded fit, after the statistics all-reduce, in one launch.
+// Blocks k >= K (padding components) only rewrite their padding operands.
+__global__ void __launch_bounds__(128)
+em_update_prep_kernel(const double *__restrict__ stats, double n_total, int K, int d,
+                      float *__restrict__ new_mu, float *__restrict__ new_var,
+                      float *__restrict__ new_log_pi, int floors, TcParamOps op) {
+  griddep_launch();
+  griddep_wait();
+  const int k = blockIdx.x, j = threadIdx.x;
+  float2 mv = make_float2(0.0f, 1.0f);
+  float lp32 = 0.0f;
+  if (k < K) {
+    const double nk = stats[k];
+    if (j < d)
+      mv = update_component(nk, stats[K + (int64_t)k * d + j], stats[K + (int64_t)K * d + (int64_t)k * d + j],
+                            n_total, floors, new_mu + (int64_t)k * d + j, new_var + (int64_t)k * d + j);
+    lp32 = (float)(floors ? log(fmax(nk / n_total, 1e-8)) : log(nk / n_total));
+    if (j == 0) new_log_pi[k] = lp32;
+  }
+  tc_prep_component(k, K, d, j, mv.x, mv.y, lp32, op, 1);
+}
+
+int em_update_prep(const double *stats, double n_total, int K, int Kp, int d, float *new_mu,
+                   float *new_var, float *new_log_pi, const TcParamOps &op, cudaStream_t stream) {
+  if (d > 128) return fail(FGMM_ERR_UNSUPPORTED, "operand preparation needs d <= 128");
+  FGMM_CUDA_TRY(launch_pdl(em_update_prep_kernel, Kp, 128, 0, stream, stats, n_total, K, d, new_mu,
+                           new_var, new_log_pi, 1, op));
+  return FGMM_OK;
+}
+
 int em_update(const double *stats, double n_total, int K, int d, float *new_mu, float *new_var,
               float *new_log_pi, cudaStream_t stream, bool floors) {
   int threads = d >= 128 ? 128 : (d >= 64 ? 64 : 32);

@@ -35,12 +35,21 @@ def _gpu_stats(X, mu, var, log_pi, state):
     if "points" not in state:
         state["points"] = C.prepare_points(X, mu.shape[0])
         state["ws"] = C.StatsWorkspace(X.shape[0], X.shape[1], mu.shape[0], X.device)
-    stats, ln = C.em_stats(X, mu, var, log_pi, points=state["points"], workspace=state["ws"])
+        state["tc"] = C.family_for(X.shape[0], X.shape[1], mu.shape[0]) == 2
+    stats, ln = C.em_stats(X, mu, var, log_pi, points=state["points"], workspace=state["ws"],
+                           prepared=state.get("prepared", False))
     return stats, ln
 
 
-def _gpu_update(stats, n_total, K, d):
+def _gpu_update(stats, n_total, K, d, state=None):
+    """The M-step after the all-reduce.  On the tensor-core family the same launch writes
+    the next step's parameter operands into this rank's workspace (one launch instead of
+    an update plus a preparation)."""
     from . import flash_gmm_native as C
+    if state is not None and state.get("tc"):
+        out = C.em_update_prepared(stats, n_total, state["points"], state["ws"])
+        state["prepared"] = True
+        return out
     return C.em_update(stats, n_total, K, d)
 
 
@@ -91,7 +100,10 @@ class DistributedFlashGMM:
             t0 = time.time()
             stats, ln = self.stats_fn(X_local, mu, var, log_pi, state)
             stats = self._allreduce(stats.clone(), it)
-            mu, var, log_pi = self.update_fn(stats, n_total, self.K, self.d)
+            if self.update_fn is _gpu_update:
+                mu, var, log_pi = self.update_fn(stats, n_total, self.K, self.d, state=state)
+            else:
+                mu, var, log_pi = self.update_fn(stats, n_total, self.K, self.d)
             avg_ll = stats[-1].item() / n_total
             if X_local.is_cuda and self.stats_fn is _gpu_stats:
                 from . import _lib

@@ -23,7 +23,7 @@ from . import _lib
 
 __all__ = ["flash_em_fused", "standard_e_step", "flash_e_step", "standard_m_step", "em_stats", "em_step",
            "StatsWorkspace",
-           "em_update", "prepare_points", "stats_len", "family_for", "set_family"]
+           "em_update", "em_update_prepared", "prepare_points", "stats_len", "family_for", "set_family"]
 
 
 def _stream_ptr(device):
@@ -189,11 +189,13 @@ class StatsWorkspace:
         self.ln = torch.empty(N, dtype=torch.float32, device=device)
 
 
-def em_stats(X, mu, var, log_pi, points=None, workspace=None):
+def em_stats(X, mu, var, log_pi, points=None, workspace=None, prepared=False):
     """Pass 1 + Pass 2 over local points -> ``(stats fp64 [K(2d+1)+1], log_normalizer[N])``.
 
     ``stats`` packs ``[n_k | s_k | sq_k | sum log_normalizer]``; sum it across ranks
-    before :func:`em_update` for a sharded fit.
+    before :func:`em_update` for a sharded fit.  ``prepared=True`` asserts that
+    :func:`em_update_prepared` produced ``mu, var, log_pi`` with this ``workspace`` and
+    ``points``, so their tensor-core operands are reused.
     """
     X, mu, var, log_pi, N, d, K = _check_params(X, mu, var, log_pi)
     lib = _lib.load()
@@ -203,11 +205,11 @@ def em_stats(X, mu, var, log_pi, points=None, workspace=None):
             workspace = StatsWorkspace(N, d, K, dev)
         if points is None and lib.fgmm_points_bytes(N, d, K) > 0:
             points = prepare_points(X, K)
-        _lib.check(lib.fgmm_em_stats(X.data_ptr(), points.data_ptr() if points is not None else None,
-                                     N, d, mu.data_ptr(), var.data_ptr(), log_pi.data_ptr(), K,
-                                     workspace.stats.data_ptr(), workspace.ln.data_ptr(),
-                                     workspace.ws.data_ptr(), workspace.ws.numel(),
-                                     _stream_ptr(dev)))
+        _lib.check(lib.fgmm_em_stats_ex(X.data_ptr(), points.data_ptr() if points is not None else None,
+                                        N, d, mu.data_ptr(), var.data_ptr(), log_pi.data_ptr(), K,
+                                        workspace.stats.data_ptr(), workspace.ln.data_ptr(),
+                                        workspace.ws.data_ptr(), workspace.ws.numel(),
+                                        STEP_PREPARED if prepared else 0, _stream_ptr(dev)))
     return workspace.stats, workspace.ln
 
 
@@ -241,6 +243,24 @@ def em_step(X, mu, var, log_pi, points=None, workspace=None, out=None, prepared=
                                     workspace.ws.data_ptr(), workspace.ws.numel(),
                                     STEP_PREPARED if prepared else 0, _stream_ptr(dev)))
     return out[0], out[1], out[2], workspace.stats, workspace.ln
+
+
+def em_update_prepared(stats, n_total, points, workspace, out=None):
+    """The update step of a sharded fit: :func:`em_update` (floored) in one launch that also
+    writes the tensor-core operands of the new parameters into ``workspace``, so the next
+    ``em_stats(..., prepared=True)`` skips preparing them.  Tensor-core family only."""
+    N, d, K, dev = workspace.key
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        if out is None:
+            out = (torch.empty(K, d, dtype=torch.float32, device=dev),
+                   torch.empty(K, d, dtype=torch.float32, device=dev),
+                   torch.empty(K, dtype=torch.float32, device=dev))
+        _lib.check(lib.fgmm_em_update_prepared(stats.data_ptr(), float(n_total), points.data_ptr(),
+                                               N, d, K, out[0].data_ptr(), out[1].data_ptr(),
+                                               out[2].data_ptr(), workspace.ws.data_ptr(),
+                                               workspace.ws.numel(), _stream_ptr(dev)))
+    return out
 
 
 def em_update(stats, n_total, K, d, out=None, floors=True):

@@ -113,6 +113,27 @@ int fgmm_em_step(const float *X, const void *points, int64_t N, int32_t d,
                  double *stats, float *log_normalizer,
                  void *workspace, size_t workspace_bytes, int32_t flags, void *stream);
 
+/* fgmm_em_stats with flags: FGMM_STEP_PREPARED reuses the parameter operands that
+ * fgmm_em_update_prepared left in `workspace` for exactly these mu / var / log_pi
+ * (tensor-core family with prepared points; otherwise FGMM_ERR_INVALID).  The per-rank
+ * statistics pass of a sharded fit; like fgmm_em_stats it replaces
+ * flash_gmm/csrc/flash_gmm_cuda.cu:418-493. */
+int fgmm_em_stats_ex(const float *X, const void *points, int64_t N, int32_t d,
+                     const float *mu, const float *var, const float *log_pi, int32_t K,
+                     double *stats, float *log_normalizer,
+                     void *workspace, size_t workspace_bytes, int32_t flags, void *stream);
+
+/* The update step of a sharded fit, after the statistics all-reduce: fgmm_em_update's
+ * M-step (floors as there, flash_gmm/csrc/flash_gmm_cuda.cu:298-322) in one launch that
+ * also writes the tensor-core operands of the new parameters into `workspace` (the
+ * fgmm_em_stats workspace of this rank's N local points), so the next
+ * fgmm_em_stats_ex(..., FGMM_STEP_PREPARED) skips preparing them.  Tensor-core family
+ * only. */
+int fgmm_em_update_prepared(const double *stats, double n_total, const void *points, int64_t N,
+                            int32_t d, int32_t K, float *new_mu, float *new_var,
+                            float *new_log_pi, void *workspace, size_t workspace_bytes,
+                            void *stream);
+
 /* One fused EM iteration on one device: stats + update.  The drop-in for the
  * reference's op `flash_em_fused(X, mu, var, log_pi, BN, BK)`
  * (flash_gmm/csrc/binding.cpp:62-76 dispatching to flash_em_fused_cuda,

@@ -275,3 +275,27 @@ def test_sharded_class_single_rank_matches_native():
     finally:
         if created:
             dist.destroy_process_group()
+
+
+def test_sharded_update_prepares_the_next_operands():
+    """The sharded fit's update (em_update_prepared: M-step plus the next operands, one
+    launch) followed by em_stats(prepared=True) gives the same bits as em_update followed
+    by em_stats preparing the operands itself."""
+    from flashgmm_b200 import flash_gmm_native as C
+    if C.family_for(2048, 128, 256) != 2:
+        pytest.skip("operand reuse is a tensor-core family feature")
+    g = load_golden("c2_slice2048")
+    dev = torch.device("cuda:0")
+    X, mu, var, lp = (torch.from_numpy(g[k]).to(dev) for k in ("X", "mu", "var", "log_pi"))
+    N, d, K = X.shape[0], X.shape[1], mu.shape[0]
+    pts = C.prepare_points(X, K)
+    ws = C.StatsWorkspace(N, d, K, dev)
+    stats, _ = C.em_stats(X, mu, var, lp, points=pts, workspace=ws)
+    stats = stats.clone()
+    a = [t.clone() for t in C.em_update_prepared(stats, N, pts, ws)]
+    sa = C.em_stats(X, *a, points=pts, workspace=ws, prepared=True)[0].clone()
+    b = [t.clone() for t in C.em_update(stats, N, K, d)]
+    ws2 = C.StatsWorkspace(N, d, K, dev)
+    sb = C.em_stats(X, *b, points=pts, workspace=ws2)[0].clone()
+    for x, y in zip(a + [sa], b + [sb]):
+        assert torch.equal(x, y)
