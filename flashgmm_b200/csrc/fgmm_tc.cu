@@ -632,6 +632,153 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
   }
 }
 
+// The same refinement with one lane per point for the per-point work, for d <= 64: the
+// (point, component) pairs to re-evaluate are listed in shared memory and taken four at a
+// time, eight lanes per pair striped over the dimensions.  It executes fewer instructions
+// than eight lanes per point repeating the per-point merge, which pays at small d (configs
+// 3 and 4: 78 -> 59 and 31 -> 23 us); at d = 128 the per-point kernel measured faster
+// (37 against 45 us at config 2).
+constexpr int kRefWarps = 8;
+constexpr int kRefPts = 16;  // points per warp (lanes 0-15; more warps in flight for small N)
+template <int DPL, bool VEC>  // dimensions per lane of a pair: ceil(d / 8); VEC: float4 loads
+__global__ void __launch_bounds__(32 * kRefWarps, DPL >= 12 ? 3 : 4)
+tc_refine_items_kernel(const float *__restrict__ X, int64_t N, int d, const float *__restrict__ sc,
+                 const float *__restrict__ mu, const double *__restrict__ lc,
+                 const float *__restrict__ part_m, const float *__restrict__ part_s,
+                 const float4 *__restrict__ part_tv, const int4 *__restrict__ part_ti, int G,
+                 float *__restrict__ ln2x, int4 *__restrict__ top_i, float4 *__restrict__ top_d,
+                 uint32_t *__restrict__ xmask, int64_t msl, float *__restrict__ ln_out,
+                 double *__restrict__ ln_part, int acc_ln) {
+  __shared__ int s_item[kRefWarps][32 * kTcTop];     // (lane << 2) | c
+  __shared__ double s_val[kRefWarps][32 * kTcTop];   // exact base-2 log-likelihoods
+  __shared__ double wsum[kRefWarps];
+  griddep_launch();
+  griddep_wait();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, sub = lane & 7;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  double acc = 0.0;
+  for (int64_t base = ((int64_t)blockIdx.x * kRefWarps + warp) * kRefPts; base < N;
+       base += (int64_t)gridDim.x * kRefWarps * kRefPts) {
+    const int64_t n = base + (lane & (kRefPts - 1));
+    const bool live = lane < kRefPts && n < N;
+    // merge the component groups' summaries: leading four and the log-sum-exp of the rest
+    float mx = -INFINITY, sm = 0.0f;
+    float b[kTcTop] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    int jx[kTcTop] = {-1, -1, -1, -1};
+    if (live) {
+      for (int g = 0; g < G; ++g) {
+        const float4 tv = __ldg(part_tv + (int64_t)g * N + n);
+        const int4 ti = __ldg(part_ti + (int64_t)g * N + n);
+        lse_merge(mx, sm, __ldg(part_m + (int64_t)g * N + n), __ldg(part_s + (int64_t)g * N + n));
+        if (ti.x >= 0) summary_push(b, jx, mx, sm, tv.x, ti.x);
+        if (ti.y >= 0) summary_push(b, jx, mx, sm, tv.y, ti.y);
+        if (ti.z >= 0) summary_push(b, jx, mx, sm, tv.z, ti.z);
+        if (ti.w >= 0) summary_push(b, jx, mx, sm, tv.w, ti.w);
+      }
+    }
+    // the components within 2^-kNear of the leader are re-evaluated (the others carry
+    // responsibilities below 2e-10 of the leader's and keep their tensor-core values);
+    // list them: item pos[c] of this warp
+    bool ex[kTcTop];
+    int pos[kTcTop];
+    int nitems = 0;
+#pragma unroll
+    for (int c = 0; c < kTcTop; ++c) {
+      ex[c] = live && jx[c] >= 0 && b[c] >= b[0] - kNear;
+      const unsigned bal = __ballot_sync(0xffffffffu, ex[c]);
+      pos[c] = nitems + __popc(bal & lt_mask);
+      if (ex[c]) s_item[warp][pos[c]] = (lane << 2) | c;
+      nitems += __popc(bal);
+    }
+    __syncwarp();
+    for (int i0 = 0; i0 < nitems; i0 += 4) {
+      const int item = i0 + (lane >> 3);
+      const bool valid = item < nitems;
+      const int code = valid ? s_item[warp][item] : 0;
+      const int pl = code >> 2, c = code & 3;
+      // the component of that lane's leading slot c
+      const int k0 = __shfl_sync(0xffffffffu, jx[0], pl), k1 = __shfl_sync(0xffffffffu, jx[1], pl);
+      const int k2 = __shfl_sync(0xffffffffu, jx[2], pl), k3 = __shfl_sync(0xffffffffu, jx[3], pl);
+      const int k = c == 0 ? k0 : (c == 1 ? k1 : (c == 2 ? k2 : k3));
+      const int64_t xrow = (base + pl) * d, krow = (int64_t)(valid ? k : 0) * d;
+      double a0 = 0.0, a1 = 0.0;  // two chains
+      if (VEC) {  // d == 8 DPL, DPL % 4 == 0, 16-byte aligned rows; lane takes float4 i * 8 + sub
+#pragma unroll
+        for (int i = 0; i < DPL / 4; ++i) {
+          const int64_t q = (int64_t)(i * 8 + sub) * 4;
+          float4 x4 = make_float4(0.f, 0.f, 0.f, 0.f), m4 = x4, s4 = x4;
+          if (valid) {
+            x4 = __ldg(reinterpret_cast<const float4 *>(X + xrow + q));
+            m4 = __ldg(reinterpret_cast<const float4 *>(mu + krow + q));
+            s4 = __ldg(reinterpret_cast<const float4 *>(sc + krow + q));
+          }
+          const double t0 = ((double)x4.x - (double)m4.x) * (double)s4.x;
+          const double t1 = ((double)x4.y - (double)m4.y) * (double)s4.y;
+          const double t2 = ((double)x4.z - (double)m4.z) * (double)s4.z;
+          const double t3 = ((double)x4.w - (double)m4.w) * (double)s4.w;
+          a0 = fma(t0, t0, a0); a1 = fma(t1, t1, a1); a0 = fma(t2, t2, a0); a1 = fma(t3, t3, a1);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) {
+          const int j = i * 8 + sub;
+          const bool in = valid && j < d;
+          const float xv = in ? __ldg(X + xrow + j) : 0.0f;
+          const float mv = in ? __ldg(mu + krow + j) : 0.0f;
+          const float sv = in ? __ldg(sc + krow + j) : 0.0f;
+          const double t = ((double)xv - (double)mv) * (double)sv;
+          if (i & 1) a1 = fma(t, t, a1); else a0 = fma(t, t, a0);
+        }
+      }
+      double pq = a0 + a1;
+#pragma unroll
+      for (int o = 4; o > 0; o >>= 1) pq += __shfl_xor_sync(0xffffffffu, pq, o);
+      if (valid && sub == 0) s_val[warp][item] = (__ldg(lc + k) - 0.5 * pq) * 1.4426950408889634;
+    }
+    __syncwarp();
+    if (live) {
+      // the sum: the rest (fp32 tensor-core values), plus the leading four (exact where
+      // re-evaluated); terms relative to the maximum in fp32, the maximum kept in fp64
+      double v[kTcTop];
+      double m = (double)mx;
+#pragma unroll
+      for (int c = 0; c < kTcTop; ++c) {
+        v[c] = ex[c] ? s_val[warp][pos[c]] : (jx[c] >= 0 ? (double)b[c] : -INFINITY);
+        m = fmax(m, v[c]);
+      }
+      const double mr = m == -INFINITY ? 0.0 : m;
+      float tot = sm * exp2f((float)((double)mx - mr));
+#pragma unroll
+      for (int c = 0; c < kTcTop; ++c) tot += exp2f((float)(v[c] - mr));
+      const float lt = log2f(tot);
+      const double ln2 = mr + (double)lt;
+      ln2x[n] = (float)ln2;
+      top_i[n] = make_int4(ex[0] ? jx[0] : -1, ex[1] ? jx[1] : -1, ex[2] ? jx[2] : -1, ex[3] ? jx[3] : -1);
+      top_d[n] = make_float4((float)(v[0] - mr) - lt, (float)(v[1] - mr) - lt, (float)(v[2] - mr) - lt,
+                             (float)(v[3] - mr) - lt);
+      // mark the point in the (component tile, slice) words of its exact components
+#pragma unroll
+      for (int c = 0; c < kTcTop; ++c)
+        if (ex[c])
+          atomicOr(xmask + ((int64_t)(jx[c] / NC2_ref) * msl + n / kSlice_ref) * NC2_ref + jx[c] % NC2_ref,
+                   1u << (n % kSlice_ref));
+      const double l = ln2 * 0.6931471805599453;
+      ln_out[n] = (float)l;
+      acc += l;
+    }
+    __syncwarp();  // s_item / s_val are reused by the next 32 points
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) wsum[warp] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < kRefWarps; ++w) t += wsum[w];
+    ln_part[blockIdx.x] = acc_ln ? ln_part[blockIdx.x] + t : t;  // chunks add up in order
+  }
+}
+
 // ------------------------------------------------------------------------- pass 2
 // Statistics GEMM S[k, f] = sum_n gamma[n, k] F[n, f] with F = [x^2 | x] (fp16 hi/lo,
 // column-scaled), the tensor-core work left once pass 1 has stored the log2-likelihood
@@ -653,7 +800,10 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
 //     (KA <= 192) the tensor pipe fills one while the other drains.
 // Every hand-off is an mbarrier; no barrier spans the CTA inside the loop.
 constexpr int kSlicePts = 32;
-constexpr int kSlicesFlush = 4;
+#ifndef FGMM_SLICES_FLUSH
+#define FGMM_SLICES_FLUSH 8
+#endif
+constexpr int kSlicesFlush = FGMM_SLICES_FLUSH;
 constexpr int kGBufs = 4;
 constexpr int kThreads2 = 512;
 constexpr int kGammaWarps = 8;
@@ -1085,7 +1235,11 @@ struct TcWs {
 };
 
 constexpr int kRefineBlocks = 8192;  // 32 points per block per sweep
-inline int refine_blocks(int64_t N) { return (int)std::min<int64_t>(kRefineBlocks, cdiv(N, 32)); }
+// Blocks of the refinement launch (and log-normalizer block sums): the per-point kernel
+// takes 32 points per block and sweep, the pair-list kernel (d <= 64) 128.
+inline int refine_blocks(int64_t N, int d) {
+  return (int)std::min<int64_t>(kRefineBlocks, (d + 7) / 8 <= 8 ? cdiv(N, 128) : cdiv(N, 32));
+}
 
 // Per-chunk buffers are sized for the first (largest) chunk; the component-group
 // partials for n_ct groups, the most any chunk uses.
@@ -1207,7 +1361,7 @@ int tc_launch_chunk(const TcPlan &p, const TcChunk &c, int64_t n0, bool first, c
   if (rc) return rc;
   {
     const float *Xc = X + n0 * p.d;
-    const int blocks = refine_blocks(c.Nc);
+    const int blocks = refine_blocks(c.Nc, p.d);
     const int dpl = (p.d + 7) / 8;
     const bool vec = p.d % 32 == 0 && reinterpret_cast<uintptr_t>(Xc) % 16 == 0;  // d = 8 DPL
     const int acc = first ? 0 : 1;
@@ -1222,12 +1376,27 @@ int tc_launch_chunk(const TcPlan &p, const TcChunk &c, int64_t n0, bool first, c
                                w.mu, w.lc, w.part_m, w.part_s, w.part_tv, w.part_ti, c.G, w.ln2x,  \
                                w.top_i, w.top_d, w.xmask, w.msl, ln + n0, w.ln_part, acc));        \
   } while (0)
-    if (dpl <= 1) FGMM_REFINE(1);
-    else if (dpl <= 2) FGMM_REFINE(2);
-    else if (dpl <= 4) FGMM_REFINE(4);
-    else if (dpl <= 8) FGMM_REFINE(8);
+#define FGMM_REFINE_ITEMS(D)                                                                       \
+  do {                                                                                             \
+    const int ib = blocks;                                                                         \
+    if (vec && (D) % 4 == 0 && 8 * (D) == p.d)                                                     \
+      FGMM_CUDA_TRY(launch_pdl(tc_refine_items_kernel<D, true>, ib, 32 * kRefWarps, 0, st, Xc,     \
+                               c.Nc, p.d, w.sc, w.mu, w.lc, w.part_m, w.part_s, w.part_tv,         \
+                               w.part_ti, c.G, w.ln2x, w.top_i, w.top_d, w.xmask, w.msl, ln + n0,  \
+                               w.ln_part, acc));                                                   \
+    else                                                                                           \
+      FGMM_CUDA_TRY(launch_pdl(tc_refine_items_kernel<D, false>, ib, 32 * kRefWarps, 0, st, Xc,    \
+                               c.Nc, p.d, w.sc, w.mu, w.lc, w.part_m, w.part_s, w.part_tv,         \
+                               w.part_ti, c.G, w.ln2x, w.top_i, w.top_d, w.xmask, w.msl, ln + n0,  \
+                               w.ln_part, acc));                                                   \
+  } while (0)
+    if (dpl <= 1) FGMM_REFINE_ITEMS(1);
+    else if (dpl <= 2) FGMM_REFINE_ITEMS(2);
+    else if (dpl <= 4) FGMM_REFINE_ITEMS(4);
+    else if (dpl <= 8) FGMM_REFINE_ITEMS(8);
     else if (dpl <= 12) FGMM_REFINE(12);
     else FGMM_REFINE(16);
+#undef FGMM_REFINE_ITEMS
 #undef FGMM_REFINE
     FGMM_LAUNCH_CHECK("tc_refine_kernel");
     mark(st, "tc_refine_kernel");
@@ -1295,7 +1464,7 @@ int tc_em_stats(const float *X, const void *points, int64_t N, int d, const floa
     if (rc) return rc;
   }
   return reduce_partials(w.partial, p.first.S, K, d, p.dp, 2 * p.dp + 4, w.ln_part,
-                         refine_blocks(p.first.Nc), stats, st, update ? &up : nullptr);
+                         refine_blocks(p.first.Nc, p.d), stats, st, update ? &up : nullptr);
 }
 
 int tc_update_prepare(const double *stats, double n_total, const void *points, int64_t N, int d,
