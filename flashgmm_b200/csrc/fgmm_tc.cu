@@ -565,6 +565,13 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
     float mx = -INFINITY, sm = 0.0f;
     float b[kTcTop] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
     int jx[kTcTop] = {-1, -1, -1, -1};
+    if (G == 1) {  // one group: its summary is already the point's
+      const float4 tv = __ldg(part_tv + nn);
+      const int4 ti = __ldg(part_ti + nn);
+      mx = __ldg(part_m + nn); sm = __ldg(part_s + nn);
+      b[0] = tv.x; b[1] = tv.y; b[2] = tv.z; b[3] = tv.w;
+      jx[0] = ti.x; jx[1] = ti.y; jx[2] = ti.z; jx[3] = ti.w;
+    } else
 #pragma unroll 2
     for (int g = 0; g < G; ++g) {
       const float4 tv = __ldg(part_tv + (int64_t)g * N + nn);
@@ -665,7 +672,13 @@ tc_refine_items_kernel(const float *__restrict__ X, int64_t N, int d, const floa
     float mx = -INFINITY, sm = 0.0f;
     float b[kTcTop] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
     int jx[kTcTop] = {-1, -1, -1, -1};
-    if (live) {
+    if (live && G == 1) {  // one group: its summary is already the point's
+      const float4 tv = __ldg(part_tv + n);
+      const int4 ti = __ldg(part_ti + n);
+      mx = __ldg(part_m + n); sm = __ldg(part_s + n);
+      b[0] = tv.x; b[1] = tv.y; b[2] = tv.z; b[3] = tv.w;
+      jx[0] = ti.x; jx[1] = ti.y; jx[2] = ti.z; jx[3] = ti.w;
+    } else if (live) {
       for (int g = 0; g < G; ++g) {
         const float4 tv = __ldg(part_tv + (int64_t)g * N + n);
         const int4 ti = __ldg(part_ti + (int64_t)g * N + n);
