@@ -613,7 +613,7 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
     const float lt = log2f(tot);
     const double ln2 = mr + (double)lt;
     if (live && sub == 0) {
-      ln2x[n] = (float)ln2;
+      ln2x[n] = (float)(ln2 - kTcGammaExp);  // the statistics pass works with gamma 2^14
       top_i[n] = make_int4(ex[0] ? jx[0] : -1, ex[1] ? jx[1] : -1, ex[2] ? jx[2] : -1, ex[3] ? jx[3] : -1);
       top_d[n] = make_float4((float)(v[0] - mr) - lt, (float)(v[1] - mr) - lt, (float)(v[2] - mr) - lt,
                              (float)(v[3] - mr) - lt);
@@ -765,7 +765,7 @@ tc_refine_items_kernel(const float *__restrict__ X, int64_t N, int d, const floa
       for (int c = 0; c < kTcTop; ++c) tot += exp2f((float)(v[c] - mr));
       const float lt = log2f(tot);
       const double ln2 = mr + (double)lt;
-      ln2x[n] = (float)ln2;
+      ln2x[n] = (float)(ln2 - kTcGammaExp);  // the statistics pass works with gamma 2^14
       top_i[n] = make_int4(ex[0] ? jx[0] : -1, ex[1] ? jx[1] : -1, ex[2] ? jx[2] : -1, ex[3] ? jx[3] : -1);
       top_d[n] = make_float4((float)(v[0] - mr) - lt, (float)(v[1] - mr) - lt, (float)(v[2] - mr) - lt,
                              (float)(v[3] - mr) - lt);
@@ -988,9 +988,10 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
           if ((xw >> p) & 1u) {
             const int4 ti = ti_s[p0 + p];
             const float4 td = td_s[p0 + p];
-            dl = kabs == ti.x ? td.x : (kabs == ti.y ? td.y : (kabs == ti.z ? td.z : td.w));
+            dl = (kabs == ti.x ? td.x : (kabs == ti.y ? td.y : (kabs == ti.z ? td.z : td.w))) +
+                 (float)kTcGammaExp;
           }
-          g[p] = p < live ? ex2(dl + (float)kTcGammaExp) : 0.0f;
+          g[p] = p < live ? ex2(dl) : 0.0f;
           nk += g[p];
         }
       }
