@@ -851,7 +851,8 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
                 const __grid_constant__ CUtensorMap tm_l, const float *__restrict__ ln2x,
                 const int4 *__restrict__ top_i, const float4 *__restrict__ top_d,
                 const uint32_t *__restrict__ xmask, int64_t msl, int64_t N, int S_slots, int K, int d,
-                const int *__restrict__ aexp, float *__restrict__ partial, int accum) {
+                const int *__restrict__ aexp, float *__restrict__ partial, int accum,
+                const float *__restrict__ Lt, int64_t Npad) {
   constexpr int KA = NKCF * 64;
   constexpr int DP = KA / 2;
   constexpr int PSTRIDE = 2 * DP + 4;
@@ -1062,14 +1063,24 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
       prefetch_tmap(&tm_flo);
       prefetch_tmap(&tm_l);
     }
-    // Lt is read exactly once
+    // Lt is read exactly once: once a slice's tile has been consumed, its lines are dropped
+    // from L2 without being written back, so a block that stayed in L2 from pass 1 to here
+    // never reaches DRAM
     const uint64_t pol_l = policy_evict_first();
+    auto discard_lt_slice = [&](int sd) {
+      const float *row0 = Lt + (int64_t)ct * NC2 * Npad + (s0 + sd) * kSlicePts;
+#pragma unroll
+      for (int r = lane; r < NC2; r += 32) discard_l2_line(row0 + (int64_t)r * Npad);
+    };
     for (int s = 0; s < S && ok; ++s) {
       // same rule as the gamma warps, NST slices ahead (before the EMPTY wait below)
       while (nf < T && s >= kSlicesFlush * (nf + 1) + NST && ok) flush_next(false);
       if (nf < T && s >= kSlicesFlush * (nf + 1) && tile_done(nf)) flush_next(false);  // early
       const int st = s % NST;
-      if (s >= NST) ok = ok && __all_sync(0xffffffffu, mbar_wait(EMPTY(st), ((s / NST) & 1) ^ 1, kErrWaitEmpty));
+      if (s >= NST) {
+        ok = ok && __all_sync(0xffffffffu, mbar_wait(EMPTY(st), ((s / NST) & 1) ^ 1, kErrWaitEmpty));
+        if (ok) discard_lt_slice(s - NST);
+      }
       if (!ok) break;
       if (lane == 0) {
         const uint32_t base = smem_u32(smem + st * Sh::kStage);
@@ -1096,6 +1107,12 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
   while (nf < T && ok) flush_next(warp > kGammaWarps + 1);
 
   ok = cta_sync_and(ok);
+  if (warp == kGammaWarps + 1 && ok) {  // the producer drops the last slices' Lt lines
+    for (int sd = (S > NST ? S - NST : 0); sd < S; ++sd) {
+      const float *row0 = Lt + (int64_t)ct * NC2 * Npad + (s0 + sd) * kSlicePts;
+      for (int r = lane; r < NC2; r += 32) discard_l2_line(row0 + (int64_t)r * Npad);
+    }
+  }
   const int k = ct * NC2 + cl;
   if (k < K) {
     float *dst = partial + ((int64_t)k * S_slots + slot) * PSTRIDE;
@@ -1353,8 +1370,7 @@ int launch_stats(const TcPlan &p, const TcChunk &c, const PtsPtrs &pp, int64_t n
   FGMM_CUDA_TRY(launch_pdl(tc_stats_kernel<NKCF>, c.grid2, kThreads2, StatsShape<KA>::kSmem, st,
                            m_fhi, m_flo, m_l, w.ln2x, w.top_i, w.top_d, w.xmask, w.msl, c.Nc, c.S,
                            p.K, p.d, pp.aexp,
-                           w.partial,
-                           first ? 0 : 1));
+                           w.partial, first ? 0 : 1, w.L, rows));
   mark(st, "tc_stats_kernel");
   return FGMM_OK;
 }

@@ -183,6 +183,11 @@ __device__ __forceinline__ void st_hint(float *p, float v, uint64_t policy) {
   asm volatile("st.global.L2::cache_hint.f32 [%0], %1, %2;" ::"l"(p), "f"(v), "l"(policy));
 }
 
+// Drops the 128-byte L2 line at p without writing it back (its data is dead).
+__device__ __forceinline__ void discard_l2_line(const void *p) {
+  asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory");
+}
+
 // 3-D tile load (same completion mechanism as tma_load_2d).
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, int32_t x,
                                             int32_t y, int32_t z, uint32_t bar) {
