@@ -837,6 +837,7 @@ struct StatsShape {
   static constexpr int kStagesFit = (220 * 1024) / kStage;
   static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
   static constexpr int kSmem = 1024 + kStages * kStage + 512;
+  static_assert(kStages * kStage >= NC2 * (KA + 4) * 4 + NC2 * 4, "partial rows staged in the ring");
 };
 
 __device__ __forceinline__ bool cta_sync_and(bool v) {
@@ -1113,35 +1114,45 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
       for (int r = lane; r < NC2; r += 32) discard_l2_line(row0 + (int64_t)r * Npad);
     }
   }
-  const int k = ct * NC2 + cl;
-  if (k < K) {
-    float *dst = partial + ((int64_t)k * S_slots + slot) * PSTRIDE;
+  // The tile's partial rows go through shared memory (the stage ring is idle now), so the
+  // global writes are whole coalesced rows: row c = component ct * 128 + c, laid out
+  // [s (DP) | sq (DP) | n | pad].  The column and responsibility scales are undone by exact
+  // power-of-two multiplies.
+  float *rows_s = reinterpret_cast<float *>(smem);         // [128][PSTRIDE]
+  float *nk_s = rows_s + NC2 * PSTRIDE;                     // [128]
 #pragma unroll
-    for (int e = 0; e < SEG; e += 4) {
-      const int f = seg * SEG + e;  // feature column: x^2 part first, then x
-      const int j0 = f < DP ? f : f - DP, t = f < DP ? 0 : 1;
-      float r[4];
+  for (int e = 0; e < SEG; e += 4) {
+    const int f = seg * SEG + e;  // feature column: x^2 part first, then x
+    const int j0 = f < DP ? f : f - DP, t = f < DP ? 0 : 1;
+    float r[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)  // undo the column scale and the responsibility scale
-        r[i] = (ok && j0 + i < d) ? ldexpf(sacc[e + i], -(__ldg(aexp + 3 * (j0 + i) + t) + kTcGammaExp))
-                                  : 0.0f;
-      float4 *o = reinterpret_cast<float4 *>(dst + (f < DP ? DP + f : f - DP));
-      float4 v = make_float4(r[0], r[1], r[2], r[3]);
+    for (int i = 0; i < 4; ++i) {
+      const int ex = (j0 + i < d ? __ldg(aexp + 3 * (j0 + i) + t) : 0) + kTcGammaExp;
+      r[i] = (ok && j0 + i < d) ? sacc[e + i] * __int_as_float((127 - ex) << 23) : 0.0f;
+    }
+    *reinterpret_cast<float4 *>(rows_s + cl * PSTRIDE + (f < DP ? DP + f : f - DP)) =
+        make_float4(r[0], r[1], r[2], r[3]);
+  }
+  // n_k: the two gamma warps of a lane quarter add up their halves of the points
+  if (warp >= 4 && warp < kGammaWarps) nk_s[cl] = nk;
+  __syncthreads();
+  if (warp < 4)
+    *reinterpret_cast<float4 *>(rows_s + cl * PSTRIDE + 2 * DP) =
+        make_float4(ok ? (nk + nk_s[cl]) * (1.0f / (float)(1 << kTcGammaExp)) : 0.0f, 0.f, 0.f, 0.f);
+  __syncthreads();
+  {
+    constexpr int Q = PSTRIDE / 4;  // float4 per row
+    const int rows = min(NC2, K - ct * NC2);
+    for (int i = threadIdx.x; i < rows * Q; i += kThreads2) {
+      const int c = i / Q, q = i - c * Q;
+      float4 *o = reinterpret_cast<float4 *>(partial + ((int64_t)(ct * NC2 + c) * S_slots + slot) * PSTRIDE) + q;
+      float4 v = reinterpret_cast<const float4 *>(rows_s + c * PSTRIDE)[q];
       if (accum) {  // a later chunk of the same iteration: this CTA slot's row adds up
         const float4 o0 = *o;
         v = make_float4(o0.x + v.x, o0.y + v.y, o0.z + v.z, o0.w + v.w);
       }
       *o = v;
     }
-  }
-  // n_k: the two gamma warps of a lane quarter add up their halves of the points
-  float *nk_s = reinterpret_cast<float *>(smem);  // [128], the stage ring is idle now
-  if (warp >= 4 && warp < kGammaWarps) nk_s[cl] = nk;
-  __syncthreads();
-  if (warp < 4 && k < K) {
-    float *o = partial + ((int64_t)k * S_slots + slot) * PSTRIDE + 2 * DP;
-    const float v = ok ? ldexpf(nk + nk_s[cl], -kTcGammaExp) : 0.0f;
-    *o = accum ? *o + v : v;
   }
   tc_fence_before();
   __syncthreads();
