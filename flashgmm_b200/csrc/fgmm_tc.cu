@@ -267,9 +267,22 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
   __syncthreads();
   tc_fence_after();
   griddep_launch();
+  // The prepared points do not change between launches: the producer starts loading the
+  // first unit's point tiles before waiting for the earlier launches (which write the
+  // parameter operands, Lt's readers and the bit words); every other thread waits first.
+  const int n_units = n_pt * G;
+  const int npre = (warp == 0 && lane == 0 && (int)blockIdx.x < n_units) ? min(S, NKC) : 0;
+  if (npre > 0) {
+    const int pt0 = blockIdx.x / G;
+    for (int c = 0; c < npre; ++c) {
+      const uint32_t base = smem_u32(smem + c * Sh::kStage);
+      mbar_arrive_expect_tx(FULL(c), Sh::kStage);
+      tma_load_2d_hint(base, &tm_phi, c * KCH, pt0 * BM, FULL(c), policy_evict_first());
+      tma_load_2d_hint(base + Sh::kPBytes, &tm_plo, c * KCH, pt0 * BM, FULL(c), policy_evict_first());
+    }
+  }
   griddep_wait();  // the parameter operands and Lt of earlier launches
   const uint32_t tmem = *tmem_slot;
-  const int n_units = n_pt * G;
 
   if (warp == 0) {
     if (lane != 0) {  // the idle lanes clear the exact-component words the refinement sets
@@ -289,9 +302,12 @@ tc_pass1_kernel(const __grid_constant__ CUtensorMap tm_phi, const __grid_constan
           for (int c = 0; c < NKC; ++c) {
             if (!mbar_wait(EMPTY(stage), phase ^ 1, kErrWaitEmpty)) { ok = false; break; }
             const uint32_t base = smem_u32(smem + stage * Sh::kStage);
-            mbar_arrive_expect_tx(FULL(stage), Sh::kStage);
-            tma_load_2d_hint(base, &tm_phi, c * KCH, pt * BM, FULL(stage), pol_p);
-            tma_load_2d_hint(base + Sh::kPBytes, &tm_plo, c * KCH, pt * BM, FULL(stage), pol_p);
+            const bool pre = u == (int)blockIdx.x && t == g * tpg && c < npre;  // P already on its way
+            if (!pre) {
+              mbar_arrive_expect_tx(FULL(stage), Sh::kStage);
+              tma_load_2d_hint(base, &tm_phi, c * KCH, pt * BM, FULL(stage), pol_p);
+              tma_load_2d_hint(base + Sh::kPBytes, &tm_plo, c * KCH, pt * BM, FULL(stage), pol_p);
+            }
             tma_load_2d_hint(base + 2 * Sh::kPBytes, &tm_qhi, c * KCH, t * NC, FULL(stage), pol_q);
             tma_load_2d_hint(base + 2 * Sh::kPBytes + Sh::kQBytes, &tm_qlo, c * KCH, t * NC,
                              FULL(stage), pol_q);
@@ -901,6 +917,16 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
   __syncthreads();
   tc_fence_after();
   griddep_launch();
+  // F (prepared points) does not change between launches: the producer starts loading the
+  // first slices' F before waiting for the earlier launches; every other thread waits first.
+  const int fpre = (warp == kGammaWarps + 1 && lane == 0) ? min(S, NST) : 0;
+  for (int sp = 0; sp < fpre; ++sp) {
+    const uint32_t base = smem_u32(smem + sp * Sh::kStage);
+    const int64_t nb = (s0 + sp) * kSlicePts;
+    mbar_arrive_expect_tx(FULL(sp), 2 * Sh::kFPart + kSlicePts * NC2 * 4 + kSlicePts * 36 + NC2 * 4);
+    tma_load_3d(base, &tm_fhi, 0, (int32_t)nb, 0, FULL(sp));
+    tma_load_3d(base + Sh::kFPart, &tm_flo, 0, (int32_t)nb, 0, FULL(sp));
+  }
   griddep_wait();  // Lt, ln2x and the partial rows of earlier launches
   const uint32_t tmem = *tmem_slot;
 
@@ -1086,10 +1112,11 @@ tc_stats_kernel(const __grid_constant__ CUtensorMap tm_fhi, const __grid_constan
       if (lane == 0) {
         const uint32_t base = smem_u32(smem + st * Sh::kStage);
         const int64_t nb = (s0 + s) * kSlicePts;
-        // F, Lt, ln2, leaders, exact-component words
-        mbar_arrive_expect_tx(FULL(st), 2 * Sh::kFPart + kSlicePts * NC2 * 4 + kSlicePts * 36 + NC2 * 4);
-        tma_load_3d(base, &tm_fhi, 0, (int32_t)nb, 0, FULL(st));
-        tma_load_3d(base + Sh::kFPart, &tm_flo, 0, (int32_t)nb, 0, FULL(st));
+        if (s >= fpre) {  // F, Lt, ln2, leaders, exact-component words (F of the first slices is on its way)
+          mbar_arrive_expect_tx(FULL(st), 2 * Sh::kFPart + kSlicePts * NC2 * 4 + kSlicePts * 36 + NC2 * 4);
+          tma_load_3d(base, &tm_fhi, 0, (int32_t)nb, 0, FULL(st));
+          tma_load_3d(base + Sh::kFPart, &tm_flo, 0, (int32_t)nb, 0, FULL(st));
+        }
         tma_load_2d_hint(base + Sh::kLOff, &tm_l, (int32_t)nb, ct * NC2, FULL(st), pol_l);
         bulk_load(base + Sh::kNOff, ln2x + nb, kSlicePts * 4, FULL(st));
         bulk_load(base + Sh::kTOff, top_i + nb, kSlicePts * 16, FULL(st));
