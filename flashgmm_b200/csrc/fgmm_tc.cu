@@ -553,7 +553,7 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
                  double *__restrict__ ln_part, int acc_ln) {
   __shared__ double wsum[8];
   griddep_launch();
-  griddep_wait();
+  bool waited = false;  // X is an input: its first rows load before waiting for pass 1
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int sub = lane & 7;  // lane within the point's group of 8
   double acc = 0.0;
@@ -576,6 +576,10 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
         const int j = i * 8 + sub;
         x[i] = j < d ? __ldg(X + nn * d + j) : 0.0f;
       }
+    }
+    if (!waited) {
+      griddep_wait();
+      waited = true;
     }
     // merge the component groups' summaries: leading four and the log-sum-exp of the rest
     float mx = -INFINITY, sm = 0.0f;
@@ -646,6 +650,7 @@ tc_refine_kernel(const float *__restrict__ X, int64_t N, int d, const float *__r
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (!waited) griddep_wait();
   if (lane == 0) wsum[warp] = acc;
   __syncthreads();
   if (threadIdx.x == 0) {
