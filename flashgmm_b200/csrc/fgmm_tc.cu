@@ -212,7 +212,8 @@ __device__ __forceinline__ void summary_push(float (&tv)[kTcTop], int (&ti)[kTcT
 // Epilogue warp w owns TMEM lane quarter w % 4 (32 points) and a quarter of the tile's
 // columns; it turns accumulators into log2-likelihoods l2 = cst2 + coef D, stores them
 // into Lt (transposed, evict_last: the statistics pass reads them back), and keeps per
-// point an online (max, sum) and the four largest l2 with their components.
+// point a summary: the four largest l2 within 2^-kNear of the point's running maximum,
+// with their components, and the log-sum-exp of the rest.
 template <int NKC, int NC>
 struct Pass1Shape {
   static constexpr int S = NC == 256 ? 2 : 3;             // stages
@@ -512,8 +513,12 @@ __device__ __forceinline__ void exact_pair(const float (&x)[DPL], int sub, int d
       }
     }
   }
+  // the second component's arithmetic only where some point of the warp needs it
+  const bool any1 = __any_sync(0xffffffffu, k1 >= 0);
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
+    p[u] = 0.0;
+    if (u == 1 && !any1) break;
     double a0 = 0.0, a1 = 0.0;  // two chains
 #pragma unroll
     for (int i = 0; i < DPL; ++i) {
@@ -816,28 +821,27 @@ tc_refine_items_kernel(const float *__restrict__ X, int64_t N, int d, const floa
 // ------------------------------------------------------------------------- pass 2
 // Statistics GEMM S[k, f] = sum_n gamma[n, k] F[n, f] with F = [x^2 | x] (fp16 hi/lo,
 // column-scaled), the tensor-core work left once pass 1 has stored the log2-likelihood
-// block Lt (with the exact leading components written over their tensor-core values).
+// block Lt and the refinement the exact leading components of every point.
 // A CTA owns 128 components (the M of the MMA, on the TMEM lanes) and a contiguous range
-// of points, taken in slices of 16 points (the K of one kind::f16 k-step).  Roles:
-//   warp 9 lane 0 (producer): per slice, TMA of F hi and F lo (one 3-D box each: 16 points
+// of points, taken in slices of 32 points (two kind::f16 k-steps).  Roles:
+//   warp 9 lane 0 (producer): per slice, TMA of F hi and F lo (one 3-D box each: 32 points
 //     x all 64-feature atoms, MN-major SWIZZLE_128B), of the slice's Lt tile
-//     [16 points][128 components] and of its 16 log2-normalizers;
-//   warps 0-7 (gamma): warp w computes gamma = 2^(l2 - ln2) for components 32 (w % 4) ..
-//     +31 (its TMEM lane quarter) at 8 of the slice's 16 points, scales it by 2^14,
-//     splits it into fp16 hi / lo and stores the pairs into a TMEM gamma buffer (two
-//     points per 32-bit column), the MMA's A operand;
-//   warp 8 lane 0 (MMA): three MMAs per slice (gamma_lo F_hi, gamma_hi F_lo, gamma_hi
-//     F_hi) into the statistics accumulator;
-//   all 16 warps: every kSlicesFlush slices (128 points) the accumulator is added into
+//     [128 components][32 points], its 32 log2-normalizers (shifted by the gamma scale),
+//     the points' exact leaders and the slice's exact-component bit words;
+//   warps 0-7 (gamma): warp w computes gamma 2^14 = 2^(l2 - ln2 + 14) for components
+//     32 (w % 4) .. +31 (its TMEM lane quarter) at 16 of the slice's 32 points, taking
+//     the exact value where the component's bit is set, splits it into fp16 hi / lo and
+//     stores the pairs into a TMEM gamma buffer (two points per 32-bit column), the MMA's
+//     A operand;
+//   warp 8 lane 0 (MMA): six MMAs per slice (gamma_lo F_hi, gamma_hi F_lo, gamma_hi F_hi,
+//     two k-steps each) into the statistics accumulator;
+//   all 16 warps: every kSlicesFlush slices (256 points) the accumulator is added into
 //     fp32 registers (warp w: lane quarter w % 4, a quarter of the columns), because
 //     tensor-memory accumulation does not round to nearest.  With two accumulator regions
 //     (KA <= 192) the tensor pipe fills one while the other drains.
 // Every hand-off is an mbarrier; no barrier spans the CTA inside the loop.
 constexpr int kSlicePts = 32;
-#ifndef FGMM_SLICES_FLUSH
-#define FGMM_SLICES_FLUSH 8
-#endif
-constexpr int kSlicesFlush = FGMM_SLICES_FLUSH;
+constexpr int kSlicesFlush = 8;  // drains every 256 points
 constexpr int kGBufs = 4;
 constexpr int kThreads2 = 512;
 constexpr int kGammaWarps = 8;

@@ -27,7 +27,6 @@ enum : int {
   kErrWaitGammaEmpty = 6,
   kErrWaitStatsDone = 7,
   kErrWaitDrain = 8,
-  kErrWaitPoints = 9,
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
