@@ -91,3 +91,23 @@ def test_top_level_module_runs_the_cuda_op():
     assert len(out) == 4 and all(o.is_cuda for o in out)
     ln = out[3].cpu().numpy()
     assert np.max(np.abs(ln - g["log_normalizer"])) < 1e-3
+
+
+def test_compiled_op_module_matches_the_c_abi_path():
+    """The compiled extension's ops (what ``import flash_gmm_native`` exports) give the same
+    bits as the ctypes binding of the same C ABI."""
+    import flash_gmm_native as top
+    from flashgmm_b200 import flash_gmm_native as C
+    g = load_golden("c2_slice2048")
+    t = [torch.from_numpy(g[k]).to(DEV) for k in ("X", "mu", "var", "log_pi")]
+    for a, b in zip(top.flash_em_fused(*t), C.flash_em_fused(*t)):
+        assert torch.equal(a, b)
+    ga, la = top.standard_e_step(*t)
+    gb, lb = C.standard_e_step(*t)
+    assert torch.equal(ga, gb) and torch.equal(la, lb)
+    fa = top.flash_e_step(*t, BK=4)
+    assert torch.equal(fa[0], gb)
+    for a, b in zip(top.standard_m_step(t[0], ga), C.standard_m_step(t[0], gb)):
+        assert torch.equal(a, b)
+    with pytest.raises(RuntimeError):
+        top.flash_em_fused(t[0].double(), *t[1:])
