@@ -83,46 +83,97 @@ __device__ __forceinline__ void split_f16f(float v, __half &hi, __half &lo) {
 }
 
 // --------------------------------------------------------------------------- prep
-// max |x_j| over the points (one thread per dimension, a row range per block).
-__global__ void __launch_bounds__(128) tc_xmax_kernel(const float *__restrict__ X, int64_t N, int d,
-                                                      uint32_t *__restrict__ xmax) {
-  const int j = threadIdx.x;
-  if (j >= d) return;
-  float m = 0.0f;
-  for (int64_t n = blockIdx.x; n < N; n += gridDim.x) m = fmaxf(m, fabsf(__ldg(X + n * d + j)));
-  atomicMax(xmax + j, __float_as_uint(m));  // non-negative floats order like their bits
+// max |x_j| over the points.  A block takes a contiguous row range; thread t owns
+// dimension t % d of rows t / d, t / d + R, ... (R = blockDim / d rows per pass), four
+// loads in flight; the block's maxima meet in shared memory before one global atomic per
+// dimension.
+__global__ void __launch_bounds__(256) tc_xmax_kernel(const float *__restrict__ X, int64_t N, int d,
+                                                      int64_t rows_per_block, uint32_t *__restrict__ xmax) {
+  __shared__ uint32_t s_max[kMaxD];
+  for (int j = threadIdx.x; j < d; j += blockDim.x) s_max[j] = 0u;
+  __syncthreads();
+  const int R = blockDim.x / d;
+  const int j = threadIdx.x % d, r = threadIdx.x / d;
+  const int64_t n0 = (int64_t)blockIdx.x * rows_per_block;
+  const int64_t n1 = n0 + rows_per_block < N ? n0 + rows_per_block : N;
+  if (r < R) {
+    float m[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    int64_t n = n0 + r;
+    for (; n + 3 * R < n1; n += 4 * R) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) m[u] = fmaxf(m[u], fabsf(__ldg(X + (n + u * R) * d + j)));
+    }
+    for (; n < n1; n += R) m[0] = fmaxf(m[0], fabsf(__ldg(X + n * d + j)));
+    // non-negative floats order like their bit patterns
+    atomicMax(s_max + j, __float_as_uint(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]))));
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < d; c += blockDim.x) atomicMax(xmax + c, s_max[c]);
 }
 
 // P[n][c] (c = 3 j + t: x^2, x, 1) and F[n][f] (f < dp: x^2, else x), scaled by the
-// column exponents and split into fp16 hi / lo; the threads of row 0 also record the
-// exponents of P.
-__global__ void tc_prep_points_kernel(const float *__restrict__ X, int64_t N, int64_t Npad, int d,
+// column exponents and split into fp16 hi / lo; block 0 also records the exponents of P.
+// A block stages kPrepRows rows of X in shared memory, next to a per-column table (source
+// dimension and kind, and the exact power of two 2^a_c: the product rounds exactly as
+// ldexpf does), and writes four columns per thread as 8-byte stores.  Rows >= N and
+// columns past the data are zero.
+constexpr int kPrepRows = 16;  // divides the 128-row padding of Npad
+__host__ __device__ inline int tc_prep_smem(int kbp, int ka, int d) {
+  return (kbp + ka) * 8 + kPrepRows * d * 4;
+}
+__global__ void __launch_bounds__(256) tc_prep_points_kernel(const float *__restrict__ X, int64_t N, int64_t Npad, int d,
                                       int kbp, int ka, const uint32_t *__restrict__ xmax,
                                       int *__restrict__ aexp, __half *__restrict__ phi,
                                       __half *__restrict__ plo, __half *__restrict__ fhi,
                                       __half *__restrict__ flo) {
-  const int W = kbp + ka, dp = ka / 2;
-  const int64_t total = Npad * W;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t n = i / W;
-    const int c = (int)(i - n * W);
+  extern __shared__ __align__(16) uint8_t prep_smem[];
+  const int W = kbp + ka, dp = ka / 2, Q = W / 4;  // columns, quads of columns per row
+  int *s_code = reinterpret_cast<int *>(prep_smem);            // j << 2 | t (t = 3: zero column)
+  float *s_scale = reinterpret_cast<float *>(prep_smem) + W;   // 2^a_c
+  float *xs = reinterpret_cast<float *>(prep_smem) + 2 * W;    // [kPrepRows][d]
+  for (int c = threadIdx.x; c < W; c += blockDim.x) {
     int j, t;
     if (c < kbp) { j = c / 3; t = c - 3 * j; }
     else { const int f = c - kbp; t = f < dp ? 0 : 1; j = t == 0 ? f : f - dp; }
     const bool in = j < d;
-    const int a = in ? tc_p_col_exp(3 * j + t, d, xmax) : 0;
-    const float x = (in && n < N) ? __ldg(X + n * d + j) : 0.0f;
-    const float v = ldexpf(t == 0 ? x * x : (t == 1 ? x : (in && n < N ? 1.0f : 0.0f)), a);
-    __half hi, lo;
-    split_f16f(v, hi, lo);
-    if (c < kbp) {
-      phi[n * kbp + c] = hi;
-      plo[n * kbp + c] = lo;
-      if (n == 0) aexp[c] = a;
-    } else {
-      fhi[n * ka + (c - kbp)] = hi;
-      flo[n * ka + (c - kbp)] = lo;
+    const int a = in ? tc_p_col_exp(3 * j + t, d, xmax) : 0;  // |a| <= 100
+    s_code[c] = in ? (j << 2 | t) : 3;
+    s_scale[c] = __int_as_float((a + 127) << 23);
+    if (blockIdx.x == 0 && c < kbp) aexp[c] = a;
+  }
+  const int64_t nd = N * (int64_t)d;
+  for (int64_t r0 = (int64_t)blockIdx.x * kPrepRows; r0 < Npad; r0 += (int64_t)gridDim.x * kPrepRows) {
+    __syncthreads();  // the table is written / the previous rows are consumed
+    for (int i = threadIdx.x; i < kPrepRows * d; i += blockDim.x) {
+      const int64_t g = r0 * d + i;
+      xs[i] = g < nd ? __ldg(X + g) : 0.0f;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < kPrepRows * Q; i += blockDim.x) {
+      const int r = i / Q, c = 4 * (i - r * Q);
+      const int64_t n = r0 + r;
+      const bool live = n < N;
+      __half h[4], l[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int code = s_code[c + u], t = code & 3;
+        const float x = xs[r * d + (code >> 2)];
+        float v = t == 0 ? x * x : (t == 1 ? x : (t == 2 ? 1.0f : 0.0f));
+        v = live ? v * s_scale[c + u] : 0.0f;
+        split_f16f(v, h[u], l[u]);
+      }
+      uint2 hv, lv;
+      hv.x = (uint32_t)__half_as_ushort(h[0]) | ((uint32_t)__half_as_ushort(h[1]) << 16);
+      hv.y = (uint32_t)__half_as_ushort(h[2]) | ((uint32_t)__half_as_ushort(h[3]) << 16);
+      lv.x = (uint32_t)__half_as_ushort(l[0]) | ((uint32_t)__half_as_ushort(l[1]) << 16);
+      lv.y = (uint32_t)__half_as_ushort(l[2]) | ((uint32_t)__half_as_ushort(l[3]) << 16);
+      if (c < kbp) {
+        *reinterpret_cast<uint2 *>(phi + n * kbp + c) = hv;
+        *reinterpret_cast<uint2 *>(plo + n * kbp + c) = lv;
+      } else {
+        *reinterpret_cast<uint2 *>(fhi + n * ka + (c - kbp)) = hv;
+        *reinterpret_cast<uint2 *>(flo + n * ka + (c - kbp)) = lv;
+      }
     }
   }
 }
@@ -1503,12 +1554,15 @@ int tc_prepare_points(const float *X, int64_t N, int d, void *points, cudaStream
   const PtsPtrs pp = pts_ptrs(points, N, d);
   FGMM_CUDA_TRY(cudaMemsetAsync(points, 0, kPtsHeader, st));
   const int sms = num_sms();
-  tc_xmax_kernel<<<(unsigned)std::min<int64_t>(N, 8 * sms), 128, 0, st>>>(X, N, d, pp.xmax);
+  {
+    const int64_t blocks = std::min<int64_t>(cdiv(N, 64), 4 * sms);
+    const int64_t rows = cdiv(N, blocks);
+    tc_xmax_kernel<<<(unsigned)cdiv(N, rows), 256, 0, st>>>(X, N, d, rows, pp.xmax);
+  }
   FGMM_LAUNCH_CHECK("tc_xmax_kernel");
   const int kbp = tc_kbp(d), ka = 2 * tc_dp(d);
-  const int64_t total = npad_of(N) * (kbp + ka);
-  const int blocks = (int)std::min<int64_t>(cdiv(total, 256), 16 * sms);
-  tc_prep_points_kernel<<<blocks, 256, 0, st>>>(X, N, npad_of(N), d, kbp, ka, pp.xmax,
+  const int blocks = (int)std::min<int64_t>(npad_of(N) / kPrepRows, 8 * sms);
+  tc_prep_points_kernel<<<blocks, 256, tc_prep_smem(kbp, ka, d), st>>>(X, N, npad_of(N), d, kbp, ka, pp.xmax,
                                                 const_cast<int *>(pp.aexp), pp.phi, pp.plo, pp.fhi,
                                                 pp.flo);
   FGMM_LAUNCH_CHECK("tc_prep_points_kernel");
