@@ -20,7 +20,7 @@ from oracle import oracle
 pytestmark = pytest.mark.gpu
 
 DEV = torch.device("cuda:0")
-SLACK = 2.0
+SLACK = 1.5  # measured worst: 1.15 (the golden E-step's responsibilities)
 
 
 def estep_f64(X, mu, var, lp):

@@ -12,11 +12,12 @@ see helpers.py).  Tolerances (one iteration):
     sq/n - mu^2, so its absolute error scales with mu^2 + var; 4e-6 ~ 2^-18 of that
     scale, what a few tens of fp32 accumulation steps leave),
     log_pi 1e-4 (absolute), log_normalizer 1e-3 (absolute).
-SLACK is 1.5 for the fp32 CUDA-core family (measured worst ratio to the
-reference's own error: 0.94) and 2.5 for the tcgen05 family (measured worst: 2.04,
-on the N=300/K=40/d=100 fixture's variance).  The tensor-core path is a 3xTF32
-evaluation whose tensor-memory accumulation is coarser than round-to-nearest; its
-errors sit at the reference's own fp32 noise level, not below it.
+SLACK is 1.5 for every family.  Measured worst ratios to the reference's own error, over
+the cases this suite runs with the slack set to 1.0 (only cases outside the absolute
+tolerance count): tensor-core 1.35 (N=127, K=129, d=31: more components than points,
+var_abs), low-K 1.37 (N=3001, K=9, d=116, var_abs), CUDA-core 1.12 (N=120,000, K=1,100,
+d=16, var_abs).  At the configuration slices the tensor-core errors stay at or below
+0.37x the reference's own.
 """
 import numpy as np
 import pytest
@@ -28,8 +29,8 @@ from oracle import oracle
 pytestmark = pytest.mark.gpu
 
 TOL = {"mu": 1e-4, "var": 1e-4, "var_abs": 4e-6, "log_pi": 1e-4, "ln": 1e-3}
-SLACK_BY_FAMILY = {"simt": 1.5, "tc": 2.5, "lowk": 1.5, "auto": 2.5}
-SLACK = 2.5
+SLACK_BY_FAMILY = {"simt": 1.5, "tc": 1.5, "lowk": 1.5, "auto": 1.5}
+SLACK = 1.5
 EM = em_golden_names()
 FAMILIES = {"auto": 0, "simt": 1, "tc": 2, "lowk": 3}
 

@@ -47,7 +47,7 @@ def test_streaming_matches_oracle_trajectory():
     """Out-of-core fit against the oracle, not only against the in-memory CUDA fit: five
     iterations from the same start, the parameters after each compared with the fp64
     restatement of the reference algorithm (``oracle.flash_em_fused_f64``) driven the
-    same way, within the absolute tolerances or 2.5x the reference algorithm's own fp32
+    same way, within the absolute tolerances or 1.5x the reference algorithm's own fp32
     error on that step (``oracle.flash_em_fused``, bit-exact with the reference op).
     X streams through the GPU in chunks of 7,000 points (three chunks, the last short)."""
     from flashgmm_b200.data import make_mixture, init_params
@@ -68,7 +68,7 @@ def test_streaming_matches_oracle_trajectory():
         e = param_errors([m.mu.cpu().numpy(), m.var.cpu().numpy(), m.log_pi.cpu().numpy(), zeros],
                          [r[0], r[1], r[2], zeros], n_k=r[4], N=N)
         ref = param_errors([own[0], own[1], own[2], zeros], [r[0], r[1], r[2], zeros], n_k=r[4], N=N)
-        bad = {k: (e[k], ref[k]) for k in tol if not (e[k] <= tol[k] or e[k] <= 2.5 * ref[k])}
+        bad = {k: (e[k], ref[k]) for k in tol if not (e[k] <= tol[k] or e[k] <= 1.5 * ref[k])}
         assert not bad, f"iteration {it}: (streaming, reference) errors vs fp64: {bad}"
         assert abs(h[0]["log_likelihood"] - float(np.mean(r[3]))) < 1e-4
         mu, var, lp = (a.astype(np.float32) for a in r[:3])
