@@ -230,27 +230,6 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::tf32, issued by one thread.
-__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                         uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::tf32: A (M rows on the TMEM lanes, one
-// 32-bit column per K element) is read from tensor memory.
-__device__ __forceinline__ void mma_tf32_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                            uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
 // D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (A and B both fp16), fp32 accumulate.
 __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                         uint32_t idesc, uint32_t accumulate) {
@@ -356,22 +335,6 @@ __device__ __forceinline__ void red_add_v4(float *p, float4 v) {
                : "memory");
 }
 
-// Round an fp32 value to tf32 (nearest, ties away); result keeps the fp32 bit layout.
-#ifdef FGMM_CVT_TF32
-__device__ __forceinline__ float to_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
-}
-#else
-// Round to the nearest tf32 value, ties away from zero (the cvt.rna.tf32.f32 rounding),
-// on the integer pipes: add half a tf32 unit to the magnitude bits and clear the 13
-// low mantissa bits.
-__device__ __forceinline__ float to_tf32(float x) {
-  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
-}
-#endif
-
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -383,12 +346,9 @@ __device__ __forceinline__ float ex2(float x) {
 // SBO>>4 [32,46), version 1 [46,48), layout type [61,64).
 //   kSw128       (2): 128-byte rows, 16-byte chunks XOR (row % 8); 8-row atoms.  Used for
 //                     the K-major operands (the TMA SWIZZLE_128B pattern).
-//   kSw128Base32 (1): 128-byte rows, 32-byte chunks XOR (row % 4); 4-row atoms.  The only
-//                     layout tcgen05 accepts for MN-major 32-bit (tf32) operands (the TMA
-//                     SWIZZLE_128B_ATOM_32B pattern).
 // LBO = byte stride between atoms along MN (MN-major; unused for swizzled K-major),
 // SBO = byte stride between atoms along the other dimension.
-constexpr uint32_t kSw128 = 2, kSw128Base32 = 1;
+constexpr uint32_t kSw128 = 2;
 __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
                                           uint32_t layout) {
   uint64_t d = 0;
@@ -408,16 +368,6 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int a_mn, int b_m
   return (1u << 4)                          // D format f32
          | (0u << 7)                        // A format f16
          | (0u << 10)                       // B format f16
-         | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
-         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-
-// Instruction descriptor, kind::tf32 with fp32 accumulate.
-// a_mn / b_mn: 1 = operand is MN-major in shared memory, 0 = K-major.
-__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, int a_mn, int b_mn) {
-  return (1u << 4)                          // D format f32
-         | (2u << 7)                        // A format tf32
-         | (2u << 10)                       // B format tf32
          | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
