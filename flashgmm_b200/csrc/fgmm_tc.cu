@@ -178,6 +178,63 @@ __global__ void __launch_bounds__(256) tc_prep_points_kernel(const float *__rest
   }
 }
 
+// The same operands for d a multiple of 64 (3 d = KBp and d = dp: no padding columns) and
+// 16-byte aligned rows.  Thread t owns the dimension quad q = t % (d / 4) of rows
+// t / (d / 4), + 256 / (d / 4), ...: its twelve P columns 12 q .. 12 q + 11 and its eight F
+// columns keep their scales in registers, x comes as one float4, and the outputs leave as
+// 8-byte stores.  Values and rounding are those of tc_prep_points_kernel.
+__global__ void __launch_bounds__(256) tc_prep_points_q_kernel(const float *__restrict__ X, int64_t N, int64_t Npad, int d,
+                                        const uint32_t *__restrict__ xmax, int *__restrict__ aexp,
+                                        __half *__restrict__ phi, __half *__restrict__ plo,
+                                        __half *__restrict__ fhi, __half *__restrict__ flo) {
+  const int nq = d / 4, rpp = blockDim.x / nq;  // quads per row, rows per pass
+  const int q = threadIdx.x % nq, r = threadIdx.x / nq;
+  const int kbp = 3 * d, ka = 2 * d;
+  float sp[12], sf[8];  // 2^a of P columns 12 q + i and of F columns (x^2 of 4 q + i, then x)
+#pragma unroll
+  for (int i = 0; i < 12; ++i) {
+    const int a = tc_p_col_exp(12 * q + i, d, xmax);
+    sp[i] = __int_as_float((a + 127) << 23);
+    if (blockIdx.x == 0 && r == 0) aexp[12 * q + i] = a;
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    sf[i] = sp[3 * i];          // x^2 of dimension 4 q + i
+    sf[4 + i] = sp[3 * i + 1];  // x
+  }
+  if (r >= rpp) return;
+  for (int64_t n = (int64_t)blockIdx.x * rpp + r; n < Npad; n += (int64_t)gridDim.x * rpp) {
+    const bool live = n < N;
+    float4 x4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (live) x4 = __ldg(reinterpret_cast<const float4 *>(X + n * d) + q);
+    const float xs[4] = {x4.x, x4.y, x4.z, x4.w};
+    __half h[20], l[20];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float x = xs[i];
+      split_f16f(x * x * sp[3 * i], h[3 * i], l[3 * i]);
+      split_f16f(x * sp[3 * i + 1], h[3 * i + 1], l[3 * i + 1]);
+      split_f16f(live ? sp[3 * i + 2] : 0.0f, h[3 * i + 2], l[3 * i + 2]);
+      split_f16f(x * x * sf[i], h[12 + i], l[12 + i]);
+      split_f16f(x * sf[4 + i], h[16 + i], l[16 + i]);
+    }
+    auto pack = [](const __half *v) {
+      uint2 u;
+      u.x = (uint32_t)__half_as_ushort(v[0]) | ((uint32_t)__half_as_ushort(v[1]) << 16);
+      u.y = (uint32_t)__half_as_ushort(v[2]) | ((uint32_t)__half_as_ushort(v[3]) << 16);
+      return u;
+    };
+    uint2 *ph = reinterpret_cast<uint2 *>(phi + n * kbp + 12 * q);
+    uint2 *pl = reinterpret_cast<uint2 *>(plo + n * kbp + 12 * q);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) { ph[i] = pack(h + 4 * i); pl[i] = pack(l + 4 * i); }
+    *reinterpret_cast<uint2 *>(fhi + n * ka + 4 * q) = pack(h + 12);
+    *reinterpret_cast<uint2 *>(flo + n * ka + 4 * q) = pack(l + 12);
+    *reinterpret_cast<uint2 *>(fhi + n * ka + d + 4 * q) = pack(h + 16);
+    *reinterpret_cast<uint2 *>(flo + n * ka + d + 4 * q) = pack(l + 16);
+  }
+}
+
 // One block of 128 threads per component (rows k >= K are padding: zero operands,
 // cst2 = -inf, so they never receive responsibility).
 __global__ void __launch_bounds__(128)
@@ -1555,12 +1612,21 @@ int tc_prepare_points(const float *X, int64_t N, int d, void *points, cudaStream
   FGMM_CUDA_TRY(cudaMemsetAsync(points, 0, kPtsHeader, st));
   const int sms = num_sms();
   {
-    const int64_t blocks = std::min<int64_t>(cdiv(N, 64), 4 * sms);
+    const int64_t blocks = std::min<int64_t>(cdiv(N, 32), 8 * sms);  // 64 warps per SM
     const int64_t rows = cdiv(N, blocks);
     tc_xmax_kernel<<<(unsigned)cdiv(N, rows), 256, 0, st>>>(X, N, d, rows, pp.xmax);
   }
   FGMM_LAUNCH_CHECK("tc_xmax_kernel");
   const int kbp = tc_kbp(d), ka = 2 * tc_dp(d);
+  if (d % 64 == 0 && reinterpret_cast<uintptr_t>(X) % 16 == 0) {  // kbp == 3 d, ka == 2 d
+    const int rpp = 256 / (d / 4);
+    const int blocks = (int)std::min<int64_t>(cdiv(npad_of(N), rpp), 8 * sms);
+    tc_prep_points_q_kernel<<<blocks, 256, 0, st>>>(X, N, npad_of(N), d, pp.xmax,
+                                                    const_cast<int *>(pp.aexp), pp.phi, pp.plo,
+                                                    pp.fhi, pp.flo);
+    FGMM_LAUNCH_CHECK("tc_prep_points_q_kernel");
+    return FGMM_OK;
+  }
   const int blocks = (int)std::min<int64_t>(npad_of(N) / kPrepRows, 8 * sms);
   tc_prep_points_kernel<<<blocks, 256, tc_prep_smem(kbp, ka, d), st>>>(X, N, npad_of(N), d, kbp, ka, pp.xmax,
                                                 const_cast<int *>(pp.aexp), pp.phi, pp.plo, pp.fhi,
