@@ -213,12 +213,9 @@ int reduce_partials(const float *partials, int slots, int K, int d, int ds, int 
     up.on = 1;
     up.tc = update->tc;
   }
-#ifndef FGMM_RED_ROWS4
-#define FGMM_RED_ROWS4 1
-#endif
   if (up.tc.kbp > 0 && !(ds % 4 == 0 && W % 4 == 0 && d <= 128 && reinterpret_cast<uintptr_t>(partials) % 16 == 0))
     return fail(FGMM_ERR_UNSUPPORTED, "fused parameter preparation needs the aligned row reduction");
-  if (up.tc.kbp > 0 || (FGMM_RED_ROWS4 && ds % 4 == 0 && W % 4 == 0 && reinterpret_cast<uintptr_t>(partials) % 16 == 0))
+  if (up.tc.kbp > 0 || (ds % 4 == 0 && W % 4 == 0 && reinterpret_cast<uintptr_t>(partials) % 16 == 0))
     FGMM_CUDA_TRY(launch_pdl(reduce_rows4_kernel, K + 1, 32 * kRed4Warps, 0, stream, partials,
                              slots, K, d, ds, W, ln_partials, ln_slots, stats, up));
   else
